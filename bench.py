@@ -1,0 +1,333 @@
+#!/usr/bin/env python
+"""Benchmark of the Gated DeltaNet hot paths on B200 (one JSON line on rank 0).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one varlen prefill of 16 sequences x 8192 tokens (131072 tokens,
+Hq=Hk=16, Hv=32, D=128, bf16 q/k/v, nonzero fp32 initial state, per-token decay
+in [0.5, 0.999]) through the reference-facing ``kernel`` entry point.
+``value`` is prefill tokens/s over all ranks with inputs resident in HBM;
+the ``decode`` object reports the batched decode step (B=512, in-place state,
+fresh q/k/v/a/b per step) in seq/s and state GB/s against the HBM roofline.
+
+Multi-GPU (torchrun, one process per GPU): every rank runs its own copy of the
+workload (weak scaling; sequences and heads are independent, so there is no
+data-path collective).  Timing is device time (CUDA events), max over ranks.
+
+``--impl reference`` times the reference's own CPU implementation of the path
+(the fp32 torch recurrence of solution/gdn_baseline_torch.py, restated in
+oracle/gdn_ref.py) on the host cores, rank 0 only, on a bounded sample.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import sys
+import time
+
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+if REPO not in sys.path:
+    sys.path.insert(0, REPO)
+
+METRIC = "prefill tokens/s; decode state GB/s (% of HBM peak)"
+UNIT = "tokens/s"
+N_SEQS, SEQ_LEN = 16, 8192
+DECODE_B, DECODE_STEPS = 512, 100
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+                "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])),
+                "source": "measured"}
+    except (OSError, KeyError, ValueError):
+        return dict(FALLBACK_PEAKS, source="fallback")
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def workload_name():
+    return f"gdn_prefill_{N_SEQS}x{SEQ_LEN}_hq16_hv32_d128"
+
+
+def base_config(n_gpus):
+    return {"workload": workload_name(), "n_seqs": N_SEQS, "seq_len": SEQ_LEN,
+            "tokens_per_gpu_step": N_SEQS * SEQ_LEN, "num_qk_heads": 16, "num_v_heads": 32,
+            "head_size": 128, "initial_state": "fp32 N(0,0.02^2)", "decay_range": [0.5, 0.999],
+            "decode_workload": f"gdn_decode_b{DECODE_B}_inplace_{DECODE_STEPS}steps",
+            "l2": "inputs larger than L2 (2.2 GB per prefill step, 1 GiB decode state)",
+            "parallelism": f"replicas{n_gpus} (sequence/head sharding, no collective)"}
+
+
+def cpu_prefill_sample(impl, budget_s, threads):
+    """Time a CPU implementation on the first tokens of one 8192-token sequence
+    (all 32 heads, nonzero state), growing the sample until ~budget_s of work."""
+    from fastaf_kernel_b200 import workloads as W
+    x = W.prefill_inputs([SEQ_LEN], seed=3, decay_range=(0.5, 0.999))
+    n = 32
+    while True:
+        cu = torch.tensor([0, n], dtype=torch.int32)
+        sl = lambda t: t[:n]
+        args = (sl(x["q"]), sl(x["k"]), sl(x["v"]), x["state"], x["A_log"], sl(x["a"]),
+                x["dt_bias"], sl(x["b"]), cu, x["scale"])
+        t0 = time.perf_counter()
+        impl(*args)
+        dt = time.perf_counter() - t0
+        if dt >= budget_s or n >= SEQ_LEN:
+            return n / dt, n, dt
+        n = min(SEQ_LEN, max(n * 2, int(n * budget_s / max(dt, 1e-3) * 1.1)))
+
+
+def reference_arm(args):
+    """The reference's CPU implementation, timed on the host cores (rank 0)."""
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    from oracle import gdn_ref
+    from fastaf_kernel_b200 import workloads as W
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    sample_tokens = 256
+    x = W.prefill_inputs([SEQ_LEN], seed=3, decay_range=(0.5, 0.999))
+    cu = torch.tensor([0, sample_tokens], dtype=torch.int32)
+    sl = lambda t: t[:sample_tokens]
+    run = lambda: gdn_ref.prefill(sl(x["q"]), sl(x["k"]), sl(x["v"]), x["state"], x["A_log"],
+                                  sl(x["a"]), x["dt_bias"], sl(x["b"]), cu, x["scale"])
+    for _ in range(args.warmup):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        run()
+    dt = time.perf_counter() - t0
+    value = sample_tokens * args.steps / dt
+    # decode: one step of 8 sequences of the batched decode workload
+    d = W.decode_inputs(8, seed=2)
+    t1 = time.perf_counter()
+    gdn_ref.decode(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"], d["dt_bias"],
+                   d["b"], d["scale"])
+    ddt = time.perf_counter() - t1
+    dec_gbs = 8 * W.bytes_per_decode_seq() / ddt / 1e9
+    sample = (f"first {sample_tokens} tokens of one {SEQ_LEN}-token sequence, 32 v-heads, "
+              f"per step")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+        "config": dict(base_config(world), cpu_sample=sample),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "impl": "oracle/gdn_ref.py (torch fp32 recurrence of "
+                                 "solution/gdn_baseline_torch.py)", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "decode": {"value": dec_gbs, "unit": "GB/s", "seq_per_s": 8 / ddt,
+                   "sample": "one decode step of 8 sequences"},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--method", choices=["auto", "chunked", "recurrent"], default="auto")
+    ap.add_argument("--cpu-budget", type=float, default=10.0,
+                    help="seconds of CPU work for the CPU baseline sample")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        return reference_arm(args)
+
+    import torch.distributed as dist
+    import fastaf_kernel_b200 as fk
+    from fastaf_kernel_b200 import _lib, workloads as W
+    from fastaf_kernel_b200.clocks import ClockSampler
+
+    rank, world, local = dist_env()
+    if world != args.gpus:
+        if world == 1 and args.gpus > 1:
+            print("--gpus > 1 needs torchrun (one process per GPU)", file=sys.stderr)
+            return 2
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    _lib.load()   # fail loudly if the CUDA library is missing
+    peaks = load_peaks()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---------------- prefill: inputs resident in HBM ----------------
+    x = W.prefill_long(seed=3 + rank, device=dev)
+    T = N_SEQS * SEQ_LEN
+    out = torch.empty((T, 32, 128), dtype=torch.bfloat16, device=dev)
+    ns = torch.empty((N_SEQS, 32, 128, 128), dtype=torch.float32, device=dev)
+
+    def prefill_step():
+        fk.kernel(x["q"], x["k"], x["v"], x["state"], x["A_log"], x["a"], x["dt_bias"],
+                  x["b"], x["cu_seqlens"], x["scale"], output=out, new_state=ns,
+                  method=args.method, validate=False)
+
+    for _ in range(args.warmup):
+        prefill_step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        evs[0].record(stream)
+        for i in range(args.steps):
+            prefill_step()
+            evs[i + 1].record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    launch_ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
+    total_ms = max_over_ranks(evs[0].elapsed_time(evs[-1]))
+    ms_per_step = total_ms / args.steps
+    value = world * T * args.steps / (total_ms / 1e3)
+    flops = T * W.prefill_flops_per_token()
+    avg_launch_s = sum(launch_ms) / len(launch_ms) / 1e3
+    achieved_tflops = flops / avg_launch_s / 1e12
+    pbytes = W.prefill_bytes(T, N_SEQS, N_SEQS)
+    roofline = {"bound": "tensor", "achieved": achieved_tflops, "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": achieved_tflops / peaks["bf16_tflops"],
+                "traffic": None, "peak_source": peaks["source"],
+                "kernel": "gdn prefill (" + args.method + ")",
+                "flops_per_launch": flops, "algorithmic_bytes_per_launch": pbytes,
+                "hbm_gbs_achieved": pbytes / avg_launch_s / 1e9,
+                "hbm_frac": pbytes / avg_launch_s / 1e9 / peaks["hbm_gbs"]}
+
+    # ---------------- decode: B=512, in place, fresh inputs per step ----------------
+    d0 = W.decode_inputs(DECODE_B, seed=2 + 1000 * rank, device=dev)
+    dstate = d0["state"]
+    dsteps = [W.decode_step_inputs(DECODE_B, seed=10_000 + s + 1000 * rank, device=dev)
+              for s in range(DECODE_STEPS)]
+    dout = torch.empty((DECODE_B, 1, 32, 128), dtype=torch.bfloat16, device=dev)
+
+    def decode_step(s):
+        st = dsteps[s % DECODE_STEPS]
+        fk.kernel_decode(st["q"], st["k"], st["v"], dstate, d0["A_log"], st["a"],
+                         d0["dt_bias"], st["b"], d0["scale"], output=dout, new_state=dstate)
+
+    for s in range(args.warmup):
+        decode_step(s)
+    torch.cuda.synchronize()
+    barrier()
+    dev0 = torch.cuda.Event(enable_timing=True)
+    dev1 = torch.cuda.Event(enable_timing=True)
+    dev0.record(stream)
+    for s in range(DECODE_STEPS):
+        decode_step(s)
+    dev1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    dec_ms = max_over_ranks(dev0.elapsed_time(dev1))
+    dec_step_s = dec_ms / 1e3 / DECODE_STEPS
+    dec_bytes = DECODE_B * W.bytes_per_decode_seq()
+    dec_gbs = dec_bytes / dec_step_s / 1e9
+    decode = {"value": world * dec_gbs, "unit": "GB/s", "per_gpu_gbs": dec_gbs,
+              "seq_per_s": world * DECODE_B / dec_step_s, "ms_per_step": dec_step_s * 1e3,
+              "steps": DECODE_STEPS,
+              "roofline": {"bound": "hbm", "achieved": dec_gbs, "peak": peaks["hbm_gbs"],
+                           "unit": "GB/s", "frac": dec_gbs / peaks["hbm_gbs"],
+                           "traffic": None, "peak_source": peaks["source"],
+                           "bytes_per_launch": dec_bytes}}
+
+    # ---------------- end to end through the public API, host buffers ----------------
+    e2e = None
+    if not args.no_e2e:
+        hx = {k: (v.cpu().pin_memory() if isinstance(v, torch.Tensor) else v) for k, v in x.items()}
+        hout = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+        hns = torch.empty(ns.shape, dtype=ns.dtype, pin_memory=True)
+        dx = {k: (torch.empty_like(v, device=dev) if isinstance(v, torch.Tensor) else v)
+              for k, v in hx.items()}
+        h2d = sum(v.numel() * v.element_size() for v in hx.values() if isinstance(v, torch.Tensor))
+        d2h = hout.numel() * hout.element_size() + hns.numel() * hns.element_size()
+
+        def e2e_step():
+            for k2, v2 in hx.items():
+                if isinstance(v2, torch.Tensor):
+                    dx[k2].copy_(v2, non_blocking=True)
+            o, n2 = fk.kernel(dx["q"], dx["k"], dx["v"], dx["state"], dx["A_log"], dx["a"],
+                              dx["dt_bias"], dx["b"], dx["cu_seqlens"], dx["scale"],
+                              output=out, new_state=ns, method=args.method, validate=False)
+            hout.copy_(o, non_blocking=True)
+            hns.copy_(n2, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        n_e2e = max(1, min(args.steps, 5))
+        e0.record(stream)
+        for _ in range(n_e2e):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e_ms = max_over_ranks(e0.elapsed_time(e1))
+        e2e = {"value": world * T * n_e2e / (e_ms / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": n_e2e,
+               "path": "pinned host -> device copies, fastaf_kernel_b200.kernel, device -> "
+                       "pinned host copies of output and new_state"}
+
+    # ---------------- CPU baseline (rank 0, one GPU only) ----------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        from oracle import c_oracle
+        threads = os.cpu_count() or 1
+        tps, n_tok, dt = cpu_prefill_sample(
+            lambda *a: c_oracle.prefill(*a, num_threads=threads), args.cpu_budget, threads)
+        cpu = {"value": tps, "unit": UNIT, "cores": threads, "kind": "port",
+               "impl": "oracle/gdn_oracle.c (fp32 recurrence, OpenMP over v-heads)",
+               "sample": f"first {n_tok} tokens of one {SEQ_LEN}-token sequence, 32 v-heads, "
+                         f"nonzero state ({dt:.1f} s)"}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic (seeded; shapes and distributions of "
+                                         "the benchmark configurations)",
+                "config": base_config(world), "roofline": roofline, "cpu_baseline": cpu,
+                "e2e": e2e, "gpu_launches": args.steps, "clocks": clk.summary(),
+                "decode": decode, "launch_ms": launch_ms}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,228 @@
+"""Reference-facing entry points: ``kernel`` (varlen prefill) and ``kernel_decode``.
+
+Drop-in for ``solution/triton/kernel.py:416-556`` of the reference: same
+positional signatures, same value-returning convention, same output shapes and
+dtypes.  Both call hand-written sm_100a CUDA kernels through the C ABI
+(include/gdn_b200.h) on the current torch CUDA stream.  There is no CPU path:
+inputs must live on a CUDA device and the library must be built.
+
+Additions over the reference, all keyword-only so the positional contract is
+unchanged:
+  * ``output=`` / ``new_state=`` preallocated destinations (the harness's
+    destination-passing style, scripts/replay_first_workload.py:113-116);
+  * ``kernel_decode(..., new_state=state)`` updates the state in place;
+  * ``method=`` chooses the prefill kernel (chunked tensor-core or recurrent).
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+
+__all__ = ["kernel", "kernel_decode", "kernel_dps", "kernel_decode_dps"]
+
+_GATE_DTYPES = {torch.float32: _lib.GDN_DTYPE_F32, torch.bfloat16: _lib.GDN_DTYPE_BF16}
+_METHODS = {"auto": _lib.GDN_PREFILL_AUTO, "chunked": _lib.GDN_PREFILL_CHUNKED,
+            "recurrent": _lib.GDN_PREFILL_RECURRENT}
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _require_cuda(name: str, t: torch.Tensor, device: torch.device) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if t.device.type != "cuda":
+        raise ValueError(f"{name} must be a CUDA tensor (there is no CPU path), got {t.device}")
+    if t.device != device:
+        raise ValueError(f"{name} is on {t.device}, expected {device}")
+
+
+def _bf16(name: str, t: torch.Tensor) -> torch.Tensor:
+    if t.dtype != torch.bfloat16:
+        raise TypeError(f"{name} must be bfloat16, got {t.dtype}")
+    return t.contiguous()
+
+
+def _gate(t: torch.Tensor) -> torch.Tensor:
+    # a/b and A_log/dt_bias are read as fp32 or bf16; anything else is cast to fp32
+    # (the reference upcasts every gate input with .float(), gdn_baseline_torch.py:42-44).
+    if t.dtype not in _GATE_DTYPES:
+        t = t.float()
+    return t.contiguous()
+
+
+def _scale(scale, D: int) -> float:
+    # solution/triton/kernel.py:438-439: a falsy scale selects 1/sqrt(D).
+    if not scale or scale == 0.0:
+        return 1.0 / math.sqrt(D)
+    return float(scale)
+
+
+def _check_cu_seqlens_host(cu: torch.Tensor, T: int) -> None:
+    if cu.numel() < 1:
+        raise ValueError("cu_seqlens must have at least one entry")
+    if int(cu[0]) != 0 or int(cu[-1]) != T:
+        raise ValueError(f"cu_seqlens must start at 0 and end at T={T}, got "
+                         f"{int(cu[0])}..{int(cu[-1])}")
+    if cu.numel() > 1 and bool((cu[1:] < cu[:-1]).any()):
+        raise ValueError("cu_seqlens must be non-decreasing")
+
+
+def kernel(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: Optional[torch.Tensor],
+           A_log: torch.Tensor, a: torch.Tensor, dt_bias: torch.Tensor, b: torch.Tensor,
+           cu_seqlens: torch.Tensor, scale: Optional[float], *,
+           output: Optional[torch.Tensor] = None, new_state: Optional[torch.Tensor] = None,
+           method: str = "auto", validate: bool = True) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Varlen Gated DeltaNet prefill (solution/triton/kernel.py:416-489).
+
+    q, k [T, Hq, D] bf16; v [T, Hv, D] bf16; state [N, Hv, D, D] fp32 k-last or
+    None; A_log, dt_bias [Hv]; a, b [T, Hv]; cu_seqlens [N+1] (any int dtype;
+    cast to int32 as the reference does, :458).  Returns
+    (output [T, Hv, D] bf16, new_state [N, Hv, D, D] fp32).
+
+    ``validate`` checks cu_seqlens on the host (start 0, end T, non-decreasing);
+    for a device-resident cu_seqlens that costs one device-to-host copy.
+    """
+    device = q.device
+    for name, t in (("q", q), ("k", k), ("v", v), ("A_log", A_log), ("a", a),
+                    ("dt_bias", dt_bias), ("b", b)):
+        _require_cuda(name, t, device)
+    if q.dim() != 3 or k.dim() != 3 or v.dim() != 3:
+        raise ValueError("q, k, v must be [T, H, D]")
+    T, Hq, D = q.shape
+    Hv = v.shape[1]
+    if k.shape != q.shape:
+        raise ValueError(f"k shape {tuple(k.shape)} must equal q shape {tuple(q.shape)}")
+    if v.shape[0] != T or v.shape[2] != D:
+        raise ValueError(f"v shape {tuple(v.shape)} does not match q {tuple(q.shape)}")
+    if a.shape != (T, Hv) or b.shape != (T, Hv):
+        raise ValueError(f"a and b must be [T, Hv] = [{T}, {Hv}]")
+    if A_log.numel() != Hv or dt_bias.numel() != Hv:
+        raise ValueError(f"A_log and dt_bias must have Hv={Hv} elements")
+    if cu_seqlens.dim() != 1:
+        raise ValueError("cu_seqlens must be 1-D")
+    N = cu_seqlens.shape[0] - 1
+    if N < 0:
+        raise ValueError("cu_seqlens must have at least one entry")
+    if validate:
+        _check_cu_seqlens_host(cu_seqlens.detach().to("cpu", torch.int64), T)
+    cu = cu_seqlens.to(device=device, dtype=torch.int32).contiguous()
+    scale = _scale(scale, D)
+
+    q, k, v = _bf16("q", q), _bf16("k", k), _bf16("v", v)
+    a, b, A_log, dt_bias = _gate(a), _gate(b), _gate(A_log), _gate(dt_bias)
+    if a.dtype != b.dtype:
+        b = b.to(a.dtype)
+    if A_log.dtype != dt_bias.dtype:
+        dt_bias = dt_bias.to(A_log.dtype)
+    if state is not None:
+        _require_cuda("state", state, device)
+        if tuple(state.shape) != (N, Hv, D, D):
+            raise ValueError(f"state must be [N, Hv, D, D] = [{N}, {Hv}, {D}, {D}]")
+        state = state.to(torch.float32).contiguous()
+    if output is None:
+        output = torch.empty((T, Hv, D), dtype=torch.bfloat16, device=device)
+    elif (output.dtype != torch.bfloat16 or tuple(output.shape) != (T, Hv, D)
+          or not output.is_contiguous() or output.device != device):
+        raise ValueError("output must be a contiguous bf16 [T, Hv, D] tensor on q's device")
+    if new_state is None:
+        new_state = torch.empty((N, Hv, D, D), dtype=torch.float32, device=device)
+    elif (new_state.dtype != torch.float32 or tuple(new_state.shape) != (N, Hv, D, D)
+          or not new_state.is_contiguous() or new_state.device != device):
+        raise ValueError("new_state must be a contiguous fp32 [N, Hv, D, D] tensor on q's device")
+    if method not in _METHODS:
+        raise ValueError(f"method must be one of {sorted(_METHODS)}")
+
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        _lib.check(lib.gdn_prefill_ex(
+            _ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias),
+            _ptr(b), _ptr(cu), N, T, Hq, Hv, D, scale, _GATE_DTYPES[a.dtype],
+            _GATE_DTYPES[A_log.dtype], _ptr(output), _ptr(new_state), _METHODS[method], stream))
+    return output, new_state
+
+
+def kernel_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                  state: Optional[torch.Tensor], A_log: torch.Tensor, a: torch.Tensor,
+                  dt_bias: torch.Tensor, b: torch.Tensor, scale: Optional[float], *,
+                  output: Optional[torch.Tensor] = None,
+                  new_state: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Single-token Gated DeltaNet decode (solution/triton/kernel.py:492-556).
+
+    q, k [B, 1, Hq, D] bf16; v [B, 1, Hv, D] bf16; a, b [B, 1, Hv];
+    state [B, Hv, D, D] fp32 or None.  Returns (output [B, 1, Hv, D] bf16,
+    new_state [B, Hv, D, D] fp32).  Pass ``new_state=state`` to update the state
+    in place (no second 2 MiB-per-sequence buffer).
+    """
+    device = q.device
+    for name, t in (("q", q), ("k", k), ("v", v), ("A_log", A_log), ("a", a),
+                    ("dt_bias", dt_bias), ("b", b)):
+        _require_cuda(name, t, device)
+    if q.dim() != 4 or q.shape[1] != 1:
+        raise ValueError("q must be [B, 1, Hq, D]")
+    B, _, Hq, D = q.shape
+    Hv = v.shape[2]
+    if k.shape != q.shape:
+        raise ValueError(f"k shape {tuple(k.shape)} must equal q shape {tuple(q.shape)}")
+    if tuple(v.shape) != (B, 1, Hv, D):
+        raise ValueError(f"v must be [B, 1, Hv, D], got {tuple(v.shape)}")
+    if a.numel() != B * Hv or b.numel() != B * Hv:
+        raise ValueError(f"a and b must be [B, 1, Hv] = [{B}, 1, {Hv}]")
+    if A_log.numel() != Hv or dt_bias.numel() != Hv:
+        raise ValueError(f"A_log and dt_bias must have Hv={Hv} elements")
+    scale = _scale(scale, D)
+    q, k, v = _bf16("q", q), _bf16("k", k), _bf16("v", v)
+    a, b, A_log, dt_bias = _gate(a), _gate(b), _gate(A_log), _gate(dt_bias)
+    if a.dtype != b.dtype:
+        b = b.to(a.dtype)
+    if A_log.dtype != dt_bias.dtype:
+        dt_bias = dt_bias.to(A_log.dtype)
+    inplace = new_state is not None and state is not None and new_state.data_ptr() == state.data_ptr()
+    if state is not None:
+        _require_cuda("state", state, device)
+        if tuple(state.shape) != (B, Hv, D, D):
+            raise ValueError(f"state must be [B, Hv, D, D] = [{B}, {Hv}, {D}, {D}]")
+        if inplace:
+            if state.dtype != torch.float32 or not state.is_contiguous():
+                raise ValueError("in-place decode needs a contiguous fp32 state")
+        else:
+            state = state.to(torch.float32).contiguous()
+    if output is None:
+        output = torch.empty((B, 1, Hv, D), dtype=torch.bfloat16, device=device)
+    elif (output.dtype != torch.bfloat16 or output.numel() != B * Hv * D
+          or not output.is_contiguous() or output.device != device):
+        raise ValueError("output must be a contiguous bf16 [B, 1, Hv, D] tensor on q's device")
+    if new_state is None:
+        new_state = torch.empty((B, Hv, D, D), dtype=torch.float32, device=device)
+    elif (new_state.dtype != torch.float32 or tuple(new_state.shape) != (B, Hv, D, D)
+          or not new_state.is_contiguous() or new_state.device != device):
+        raise ValueError("new_state must be a contiguous fp32 [B, Hv, D, D] tensor on q's device")
+
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        _lib.check(lib.gdn_decode(
+            _ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias),
+            _ptr(b), B, Hq, Hv, D, scale, _GATE_DTYPES[a.dtype], _GATE_DTYPES[A_log.dtype],
+            _ptr(output), _ptr(new_state), stream))
+    return output, new_state
+
+
+def kernel_dps(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state):
+    """Destination-passing prefill: ``runnable(*inputs, *outputs)``
+    (scripts/replay_first_workload.py:113-116)."""
+    kernel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale,
+           output=output, new_state=new_state)
+
+
+def kernel_decode_dps(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state):
+    """Destination-passing decode; ``new_state`` may be ``state`` (in place)."""
+    kernel_decode(q, k, v, state, A_log, a, dt_bias, b, scale, output=output,
+                  new_state=new_state)

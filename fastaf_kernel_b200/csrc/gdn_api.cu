@@ -1,0 +1,137 @@
+// gdn_api.cu -- the C ABI declared in include/gdn_b200.h.
+//
+// Validates arguments on the host (the reference does no validation; its
+// harness maps Python exceptions to RUNTIME_ERROR, scripts/run_local_modify.py:280-286),
+// selects the kernel and launches it on the caller's stream.  Nothing here
+// allocates device memory or synchronizes.
+#include <cstdarg>
+#include <cstdio>
+#include <cmath>
+#include <cstring>
+
+#include "gdn_b200.h"
+#include "gdn_common.cuh"
+#include "gdn_launch.h"
+
+namespace {
+
+thread_local char g_last_error[512] = "";
+
+int fail(int code, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool ranges_overlap(const void *a, size_t na, const void *b, size_t nb) {
+    const auto x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
+    return x < y + nb && y < x + na;
+}
+
+int check_common(int Hq, int Hv, int D, int gate_dtype, int param_dtype, const void *q,
+                 const void *k, const void *v, const void *A_log, const void *a,
+                 const void *dt_bias, const void *b, const void *out, const float *new_state) {
+    if (D != gdn::kHeadDim)
+        return fail(GDN_ERR_UNSUPPORTED, "head_size=%d is not supported (only 128)", D);
+    if (Hq <= 0 || Hv <= 0 || Hv % Hq != 0)
+        return fail(GDN_ERR_INVALID_ARGUMENT,
+                    "num_v_heads=%d must be a positive multiple of num_qk_heads=%d", Hv, Hq);
+    if ((gate_dtype != GDN_DTYPE_F32 && gate_dtype != GDN_DTYPE_BF16) ||
+        (param_dtype != GDN_DTYPE_F32 && param_dtype != GDN_DTYPE_BF16))
+        return fail(GDN_ERR_INVALID_ARGUMENT, "gate_dtype/param_dtype must be 0 (f32) or 1 (bf16)");
+    if (!q || !k || !v || !A_log || !a || !dt_bias || !b || !out || !new_state)
+        return fail(GDN_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || !aligned16(new_state))
+        return fail(GDN_ERR_INVALID_ARGUMENT, "q/k/v/output/new_state must be 16-byte aligned");
+    return GDN_OK;
+}
+
+int cuda_status(cudaError_t e, const char *what) {
+    if (e == cudaSuccess) return GDN_OK;
+    return fail(GDN_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *gdn_last_error(void) { return g_last_error; }
+
+const char *gdn_version(void) { return "gdn_b200 0.1.0 sm_100a"; }
+
+int gdn_decode(const void *q, const void *k, const void *v, const float *state,
+               const void *A_log, const void *a, const void *dt_bias, const void *b,
+               int64_t batch, int num_qk_heads, int num_v_heads, int head_size, float scale,
+               int gate_dtype, int param_dtype, void *output, float *new_state,
+               void *stream) {
+    g_last_error[0] = '\0';
+    int rc = check_common(num_qk_heads, num_v_heads, head_size, gate_dtype, param_dtype, q, k, v,
+                          A_log, a, dt_bias, b, output, new_state);
+    if (rc) return rc;
+    if (batch < 0) return fail(GDN_ERR_INVALID_ARGUMENT, "batch=%lld < 0", (long long)batch);
+    const size_t state_bytes = static_cast<size_t>(batch) * num_v_heads * head_size * head_size * 4;
+    if (state) {
+        if (!aligned16(state)) return fail(GDN_ERR_INVALID_ARGUMENT, "state must be 16-byte aligned");
+        if (state != new_state && ranges_overlap(state, state_bytes, new_state, state_bytes))
+            return fail(GDN_ERR_INVALID_ARGUMENT,
+                        "new_state partially overlaps state (only exact aliasing is allowed)");
+    }
+    if (batch == 0) return GDN_OK;
+    gdn::DecodeArgs p{q, k, v, state, A_log, a, dt_bias, b, batch, num_qk_heads, num_v_heads,
+                      scale == 0.0f ? 1.0f / sqrtf(static_cast<float>(head_size)) : scale,
+                      gate_dtype, param_dtype, output, new_state};
+    return cuda_status(gdn::launch_decode(p, static_cast<cudaStream_t>(stream)), "gdn_decode launch");
+}
+
+int gdn_prefill_ex(const void *q, const void *k, const void *v, const float *state,
+                   const void *A_log, const void *a, const void *dt_bias, const void *b,
+                   const int32_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
+                   int num_qk_heads, int num_v_heads, int head_size, float scale,
+                   int gate_dtype, int param_dtype, void *output, float *new_state,
+                   int method, void *stream) {
+    g_last_error[0] = '\0';
+    int rc = check_common(num_qk_heads, num_v_heads, head_size, gate_dtype, param_dtype, q, k, v,
+                          A_log, a, dt_bias, b, output, new_state);
+    if (rc) return rc;
+    if (num_seqs < 0 || total_tokens < 0)
+        return fail(GDN_ERR_INVALID_ARGUMENT, "num_seqs and total_tokens must be >= 0");
+    if (total_tokens >= (int64_t(1) << 31))
+        return fail(GDN_ERR_INVALID_ARGUMENT, "total_tokens must fit in int32 (cu_seqlens is int32)");
+    if (!cu_seqlens) return fail(GDN_ERR_INVALID_ARGUMENT, "null cu_seqlens");
+    const size_t state_bytes = static_cast<size_t>(num_seqs) * num_v_heads * head_size * head_size * 4;
+    if (state) {
+        if (!aligned16(state)) return fail(GDN_ERR_INVALID_ARGUMENT, "state must be 16-byte aligned");
+        if (ranges_overlap(state, state_bytes, new_state, state_bytes))
+            return fail(GDN_ERR_INVALID_ARGUMENT, "prefill new_state must not overlap state");
+    }
+    if (method != GDN_PREFILL_AUTO && method != GDN_PREFILL_CHUNKED && method != GDN_PREFILL_RECURRENT)
+        return fail(GDN_ERR_INVALID_ARGUMENT, "unknown prefill method %d", method);
+    if (num_seqs == 0) return GDN_OK;
+    gdn::PrefillArgs p{q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs, total_tokens,
+                       num_qk_heads, num_v_heads,
+                       scale == 0.0f ? 1.0f / sqrtf(static_cast<float>(head_size)) : scale,
+                       gate_dtype, param_dtype, output, new_state};
+    const auto s = static_cast<cudaStream_t>(stream);
+    const bool chunked_ok = gdn::prefill_chunked_supported(p);
+    if (method == GDN_PREFILL_CHUNKED && !chunked_ok)
+        return fail(GDN_ERR_UNSUPPORTED, "the chunked tensor-core prefill is not available here");
+    if (method == GDN_PREFILL_RECURRENT || (method == GDN_PREFILL_AUTO && !chunked_ok))
+        return cuda_status(gdn::launch_prefill_recurrent(p, s), "gdn_prefill (recurrent) launch");
+    return cuda_status(gdn::launch_prefill_chunked(p, s), "gdn_prefill (chunked) launch");
+}
+
+int gdn_prefill(const void *q, const void *k, const void *v, const float *state,
+                const void *A_log, const void *a, const void *dt_bias, const void *b,
+                const int32_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
+                int num_qk_heads, int num_v_heads, int head_size, float scale, int gate_dtype,
+                int param_dtype, void *output, float *new_state, void *stream) {
+    return gdn_prefill_ex(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs,
+                          total_tokens, num_qk_heads, num_v_heads, head_size, scale, gate_dtype,
+                          param_dtype, output, new_state, GDN_PREFILL_AUTO, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,51 @@
+// gdn_common.cuh -- shared device helpers for the Gated DeltaNet kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gdn {
+
+constexpr int kHeadDim = 128;  // the only head size the kernels are built for
+
+// Element types of the gate inputs (a, b) and parameters (A_log, dt_bias);
+// the codes match GDN_DTYPE_F32 / GDN_DTYPE_BF16 of the C ABI.
+__device__ __forceinline__ float load_scalar(const void *p, int64_t i, int dtype) {
+    return dtype == 1 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p)[i])
+                      : reinterpret_cast<const float *>(p)[i];
+}
+
+// torch.nn.functional.softplus(x) with beta=1, threshold=20: the gate formula
+// of solution/gdn_baseline_torch.py:43 (the Triton helper at
+// solution/triton/kernel.py:107-119 differs only below x=-20).
+__device__ __forceinline__ float softplus_torch(float x) {
+    return x > 20.0f ? x : log1pf(expf(x));
+}
+
+// log(alpha) = -exp(A_log) * softplus(a + dt_bias)  (solution/gdn_baseline_torch.py:42-43)
+__device__ __forceinline__ float log_decay(float exp_A_log, float a, float dt_bias) {
+    return -exp_A_log * softplus_torch(a + dt_bias);
+}
+
+// beta = sigmoid(b)  (solution/gdn_baseline_torch.py:44)
+__device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+__device__ __forceinline__ float bf16_lo(uint32_t packed) {
+    return __uint_as_float(packed << 16);
+}
+__device__ __forceinline__ float bf16_hi(uint32_t packed) {
+    return __uint_as_float(packed & 0xffff0000u);
+}
+
+// Round-to-nearest-even fp32 -> bf16, two values packed (lo in bits 0-15).
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// Streaming (evict-first) 128-bit global accesses for data touched once.
+__device__ __forceinline__ float4 ld_stream(const float4 *p) { return __ldcs(p); }
+__device__ __forceinline__ void st_stream(float4 *p, float4 v) { __stcs(p, v); }
+
+}  // namespace gdn

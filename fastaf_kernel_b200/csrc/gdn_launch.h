@@ -1,0 +1,40 @@
+// gdn_launch.h -- internal launch interface between the C ABI (gdn_api.cu) and
+// the kernels.  Arguments are already validated when these are called.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gdn {
+
+struct DecodeArgs {
+    const void *q, *k, *v;       // bf16 [B, Hq|Hv, D]
+    const float *state;          // fp32 [B, Hv, D, D] or nullptr
+    const void *A_log, *a, *dt_bias, *b;
+    int64_t batch;
+    int Hq, Hv;
+    float scale;
+    int gate_dtype, param_dtype;
+    void *out;                   // bf16 [B, Hv, D]
+    float *new_state;            // may equal state
+};
+
+struct PrefillArgs {
+    const void *q, *k, *v;       // bf16 [T, Hq|Hv, D]
+    const float *state;          // fp32 [N, Hv, D, D] or nullptr
+    const void *A_log, *a, *dt_bias, *b;
+    const int32_t *cu_seqlens;   // [N+1], device
+    int64_t num_seqs, total_tokens;
+    int Hq, Hv;
+    float scale;
+    int gate_dtype, param_dtype;
+    void *out;                   // bf16 [T, Hv, D]
+    float *new_state;            // fp32 [N, Hv, D, D]
+};
+
+cudaError_t launch_decode(const DecodeArgs &p, cudaStream_t stream);
+cudaError_t launch_prefill_recurrent(const PrefillArgs &p, cudaStream_t stream);
+cudaError_t launch_prefill_chunked(const PrefillArgs &p, cudaStream_t stream);
+bool prefill_chunked_supported(const PrefillArgs &p);
+
+}  // namespace gdn

@@ -1,0 +1,124 @@
+/*
+ * gdn_b200.h -- C ABI of the B200 (sm_100a) Gated DeltaNet prefill/decode library.
+ *
+ * The library (libgdn_b200.so) exposes the two hot paths of the gated delta
+ * rule with a k-last fp32 recurrent state:
+ *
+ *   S_t = alpha_t * S_{t-1} (I - beta_t k_t k_t^T) + beta_t v_t k_t^T,
+ *   o_t = scale * S_t q_t,
+ *   alpha = exp(-exp(A_log) * softplus(a + dt_bias)),  beta = sigmoid(b),
+ *
+ * with q/k heads shared by Hv/Hq consecutive v-heads (GVA).
+ *
+ * All tensor arguments are raw DEVICE pointers to contiguous row-major
+ * buffers; no framework types cross this boundary.  Every entry point is
+ * asynchronous on `stream` (a cudaStream_t; NULL = legacy default stream) and
+ * returns GDN_OK or a negative status; gdn_last_error() gives the message of
+ * the calling thread's last failure.
+ */
+#ifndef GDN_B200_H_
+#define GDN_B200_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define GDN_API __attribute__((visibility("default")))
+#else
+#define GDN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define GDN_OK 0
+#define GDN_ERR_INVALID_ARGUMENT (-1) /* shape, dtype, pointer or alignment error */
+#define GDN_ERR_UNSUPPORTED (-2)      /* valid but not implemented (e.g. head size) */
+#define GDN_ERR_CUDA (-3)             /* a CUDA runtime/driver call failed */
+
+/* Element type codes for the gate inputs (a, b) and parameters (A_log, dt_bias). */
+#define GDN_DTYPE_F32 0
+#define GDN_DTYPE_BF16 1
+
+/* Prefill kernel choice for gdn_prefill_ex(). */
+#define GDN_PREFILL_AUTO 0      /* chunked tensor-core kernel when supported */
+#define GDN_PREFILL_CHUNKED 1   /* chunked (C=64) WY/UT kernel on tcgen05 tensor cores */
+#define GDN_PREFILL_RECURRENT 2 /* token-serial CUDA-core kernel */
+
+/*
+ * Varlen chunked prefill.
+ *
+ * Replaces the reference entry point
+ *   kernel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale)
+ *   -> (output, new_state)                     solution/triton/kernel.py:416-489
+ * whose outputs the caller now passes in (destination-passing style, the
+ * convention of scripts/replay_first_workload.py:113-116).
+ *
+ *   q, k        bf16 [T, Hq, D]          (Hk == Hq)
+ *   v           bf16 [T, Hv, D]
+ *   state       fp32 [N, Hv, D, D] k-last ([.., V, K]) or NULL for a zero state
+ *   A_log       [Hv]      (param_dtype)
+ *   a, b        [T, Hv]   (gate_dtype)
+ *   dt_bias     [Hv]      (param_dtype)
+ *   cu_seqlens  int32 [N+1], non-decreasing, cu_seqlens[0] = 0, cu_seqlens[N] = T
+ *   scale       0 selects 1/sqrt(D) (solution/triton/kernel.py:438-439)
+ *   output      bf16 [T, Hv, D]
+ *   new_state   fp32 [N, Hv, D, D]; must not overlap `state`.  A sequence of
+ *               length 0 gets a zero new state (solution/gdn_baseline_torch.py:61-62).
+ *
+ * Requirements: D == 128, Hv % Hq == 0, 16-byte aligned q/k/v/output/state
+ * pointers.  cu_seqlens is read on the device; entries outside [0, T] or
+ * decreasing are a caller error (the kernels clamp them so they never read or
+ * write out of bounds).
+ */
+GDN_API int gdn_prefill(const void *q, const void *k, const void *v, const float *state,
+                const void *A_log, const void *a, const void *dt_bias, const void *b,
+                const int32_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
+                int num_qk_heads, int num_v_heads, int head_size, float scale,
+                int gate_dtype, int param_dtype, void *output, float *new_state,
+                void *stream);
+
+/* gdn_prefill with an explicit kernel choice (GDN_PREFILL_*).  Same contract. */
+GDN_API int gdn_prefill_ex(const void *q, const void *k, const void *v, const float *state,
+                   const void *A_log, const void *a, const void *dt_bias, const void *b,
+                   const int32_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
+                   int num_qk_heads, int num_v_heads, int head_size, float scale,
+                   int gate_dtype, int param_dtype, void *output, float *new_state,
+                   int method, void *stream);
+
+/*
+ * Single-token decode.
+ *
+ * Replaces the reference entry point
+ *   kernel_decode(q, k, v, state, A_log, a, dt_bias, b, scale)
+ *   -> (output, new_state)                     solution/triton/kernel.py:492-556
+ *
+ *   q, k        bf16 [B, 1, Hq, D]
+ *   v           bf16 [B, 1, Hv, D]
+ *   state       fp32 [B, Hv, D, D] k-last, or NULL for a zero state
+ *   a, b        [B, 1, Hv] (gate_dtype);  A_log, dt_bias [Hv] (param_dtype)
+ *   output      bf16 [B, 1, Hv, D]
+ *   new_state   fp32 [B, Hv, D, D]; may be the same pointer as `state` (in-place
+ *               update: every element is read before it is written, by the same
+ *               thread), but must not partially overlap it.
+ *
+ * Requirements: D == 128, Hv % Hq == 0, 16-byte aligned q/k/v/state/new_state.
+ */
+GDN_API int gdn_decode(const void *q, const void *k, const void *v, const float *state,
+               const void *A_log, const void *a, const void *dt_bias, const void *b,
+               int64_t batch, int num_qk_heads, int num_v_heads, int head_size,
+               float scale, int gate_dtype, int param_dtype, void *output,
+               float *new_state, void *stream);
+
+/* Message describing the calling thread's most recent failed call ("" if none). */
+GDN_API const char *gdn_last_error(void);
+
+/* Library version string, e.g. "gdn_b200 0.1.0 sm_100a". */
+GDN_API const char *gdn_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN_B200_H_ */
