@@ -17,6 +17,7 @@ GDN_OK = 0
 GDN_ERR_INVALID_ARGUMENT = -1
 GDN_ERR_UNSUPPORTED = -2
 GDN_ERR_CUDA = -3
+GDN_ERR_DEVICE_TIMEOUT = -4
 
 GDN_DTYPE_F32 = 0
 GDN_DTYPE_BF16 = 1
@@ -26,8 +27,8 @@ GDN_PREFILL_CHUNKED = 1
 GDN_PREFILL_RECURRENT = 2
 
 # Every symbol include/gdn_b200.h declares.
-EXPORTED_SYMBOLS = ("gdn_prefill", "gdn_prefill_ex", "gdn_decode", "gdn_last_error",
-                    "gdn_version")
+EXPORTED_SYMBOLS = ("gdn_prefill", "gdn_prefill_ex", "gdn_decode", "gdn_device_status",
+                    "gdn_last_error", "gdn_version")
 
 _lock = threading.Lock()
 _lib = None
@@ -69,6 +70,8 @@ def load() -> ctypes.CDLL:
         lib.gdn_decode.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i64, i32, i32, i32, f32,
                                    i32, i32, vp, vp, vp]
         lib.gdn_decode.restype = i32
+        lib.gdn_device_status.argtypes = [vp]
+        lib.gdn_device_status.restype = i32
         lib.gdn_last_error.argtypes = []
         lib.gdn_last_error.restype = ctypes.c_char_p
         lib.gdn_version.argtypes = []

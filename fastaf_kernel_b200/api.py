@@ -23,7 +23,7 @@ import torch
 
 from . import _lib
 
-__all__ = ["kernel", "kernel_decode", "kernel_dps", "kernel_decode_dps"]
+__all__ = ["kernel", "kernel_decode", "kernel_dps", "kernel_decode_dps", "device_status"]
 
 _GATE_DTYPES = {torch.float32: _lib.GDN_DTYPE_F32, torch.bfloat16: _lib.GDN_DTYPE_BF16}
 _METHODS = {"auto": _lib.GDN_PREFILL_AUTO, "chunked": _lib.GDN_PREFILL_CHUNKED,
@@ -226,3 +226,11 @@ def kernel_decode_dps(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_s
     """Destination-passing decode; ``new_state`` may be ``state`` (in place)."""
     kernel_decode(q, k, v, state, A_log, a, dt_bias, b, scale, output=output,
                   new_state=new_state)
+
+
+def device_status(device: Optional[torch.device] = None) -> None:
+    """Synchronize the current stream and raise if a kernel timed out on a
+    bounded device-side wait since the last check (the flag is then cleared)."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    with torch.cuda.device(device):
+        _lib.check(_lib.load().gdn_device_status(torch.cuda.current_stream(device).cuda_stream))

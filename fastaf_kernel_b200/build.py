@@ -18,9 +18,12 @@ REPO_DIR = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_DIR = os.path.join(PKG_DIR, "lib")
 LIB_PATH = os.path.join(LIB_DIR, "libgdn_b200.so")
+SELFTEST_LIB_PATH = os.path.join(LIB_DIR, "libgdn_b200_selftest.so")
 INCLUDE = os.path.join(REPO_DIR, "include")
 
 SOURCES = ["gdn_api.cu", "gdn_decode.cu", "gdn_prefill_recurrent.cu", "gdn_prefill_chunked.cu"]
+# Known-answer checks of the tcgen05/TMA primitives, a separate test library.
+SELFTEST_SOURCES = ["gdn_selftest.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -40,12 +43,19 @@ def _stale(target: str, deps: List[str]) -> bool:
 
 
 def build(force: bool = False, verbose: bool = False, extra: Optional[List[str]] = None) -> str:
-    """Compile every .cu under csrc/ into lib/libgdn_b200.so (skips if up to date)."""
-    srcs = [os.path.join(CSRC, s) for s in SOURCES]
+    """Compile the product library and the primitive self-test library (skips if up to date)."""
+    _build_lib(LIB_PATH, SOURCES, force, verbose, extra)
+    _build_lib(SELFTEST_LIB_PATH, SELFTEST_SOURCES, force, verbose, extra)
+    return LIB_PATH
+
+
+def _build_lib(lib_path: str, sources: List[str], force: bool, verbose: bool,
+               extra: Optional[List[str]]) -> str:
+    srcs = [os.path.join(CSRC, s) for s in sources]
     deps = srcs + [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cuh", ".h"))]
     deps.append(os.path.join(INCLUDE, "gdn_b200.h"))
-    if not force and not _stale(LIB_PATH, deps):
-        return LIB_PATH
+    if not force and not _stale(lib_path, deps):
+        return lib_path
     os.makedirs(LIB_DIR, exist_ok=True)
     obj_dir = os.path.join(LIB_DIR, "_obj")
     os.makedirs(obj_dir, exist_ok=True)
@@ -65,14 +75,14 @@ def build(force: bool = False, verbose: bool = False, extra: Optional[List[str]]
         if r.returncode != 0:
             raise RuntimeError(f"nvcc failed on {os.path.basename(s)}")
         objs.append(o)
-    tmp = LIB_PATH + ".tmp"
+    tmp = lib_path + ".tmp"
     cmd = [nvcc, "-shared", "-o", tmp] + objs + ARCH_FLAGS + ["-Xcompiler", "-fPIC"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         sys.stderr.write(r.stdout + r.stderr)
         raise RuntimeError("nvcc link failed")
-    os.replace(tmp, LIB_PATH)
-    return LIB_PATH
+    os.replace(tmp, lib_path)
+    return lib_path
 
 
 if __name__ == "__main__":

@@ -63,6 +63,20 @@ const char *gdn_last_error(void) { return g_last_error; }
 
 const char *gdn_version(void) { return "gdn_b200 0.1.0 sm_100a"; }
 
+int gdn_device_status(void *stream) {
+    g_last_error[0] = '\0';
+    int code = 0;
+    const cudaError_t e = gdn::read_chunked_device_error(static_cast<cudaStream_t>(stream), &code, true);
+    if (e != cudaSuccess) return cuda_status(e, "gdn_device_status");
+    int rec[4] = {0, 0, 0, 0};
+    if (gdn::read_chunked_check_record(static_cast<cudaStream_t>(stream), rec) == cudaSuccess && rec[3] != 0)
+        return fail(GDN_ERR_DEVICE_TIMEOUT, "address check failed at site %d value %lld (%d failures)",
+                    rec[0], (long long)(((int64_t)rec[2] << 32) | (uint32_t)rec[1]), rec[3]);
+    if (code != 0)
+        return fail(GDN_ERR_DEVICE_TIMEOUT, "a prefill CTA timed out waiting at site %d", code);
+    return GDN_OK;
+}
+
 int gdn_decode(const void *q, const void *k, const void *v, const float *state,
                const void *A_log, const void *a, const void *dt_bias, const void *b,
                int64_t batch, int num_qk_heads, int num_v_heads, int head_size, float scale,

@@ -36,5 +36,7 @@ cudaError_t launch_decode(const DecodeArgs &p, cudaStream_t stream);
 cudaError_t launch_prefill_recurrent(const PrefillArgs &p, cudaStream_t stream);
 cudaError_t launch_prefill_chunked(const PrefillArgs &p, cudaStream_t stream);
 bool prefill_chunked_supported(const PrefillArgs &p);
+cudaError_t read_chunked_device_error(cudaStream_t stream, int *code, bool clear);
+cudaError_t read_chunked_check_record(cudaStream_t stream, int rec[4]);
 
 }  // namespace gdn

@@ -36,6 +36,7 @@ extern "C" {
 #define GDN_ERR_INVALID_ARGUMENT (-1) /* shape, dtype, pointer or alignment error */
 #define GDN_ERR_UNSUPPORTED (-2)      /* valid but not implemented (e.g. head size) */
 #define GDN_ERR_CUDA (-3)             /* a CUDA runtime/driver call failed */
+#define GDN_ERR_DEVICE_TIMEOUT (-4)   /* a kernel gave up on a bounded barrier wait */
 
 /* Element type codes for the gate inputs (a, b) and parameters (A_log, dt_bias). */
 #define GDN_DTYPE_F32 0
@@ -110,6 +111,15 @@ GDN_API int gdn_decode(const void *q, const void *k, const void *v, const float 
                int64_t batch, int num_qk_heads, int num_v_heads, int head_size,
                float scale, int gate_dtype, int param_dtype, void *output,
                float *new_state, void *stream);
+
+/*
+ * Synchronizes `stream` and reports whether any chunked-prefill kernel since the
+ * last call gave up on a bounded barrier wait (GDN_ERR_DEVICE_TIMEOUT; the flag
+ * is cleared).  The kernels never spin unboundedly: a wait that times out
+ * records its site here, drains its in-flight copies and exits.  No counterpart
+ * in the reference (its Triton kernels have no device-side waits).
+ */
+GDN_API int gdn_device_status(void *stream);
 
 /* Message describing the calling thread's most recent failed call ("" if none). */
 GDN_API const char *gdn_last_error(void);
