@@ -1,0 +1,75 @@
+// gdn_chunk_common.cuh -- pieces of the chunked (C = 64) prefill shared by its kernels:
+// bf16 hi/lo splitting, swizzled shared-memory tile addressing, and the blocked
+// 64x64 unit-lower-triangular inverse.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace gdn {
+
+// x = hi + lo with hi = bf16(x) and lo = bf16(x - hi): ~16 significant bits in two bf16.
+__device__ __forceinline__ void split_bf16(float x, float &hi, float &lo) {
+    hi = __bfloat162float(__float2bfloat16_rn(x));
+    lo = x - hi;
+}
+
+// Byte offset of element (row, col) of a bf16 tile whose rows are `kRowBytes`
+// long (128 or 256), with the 16-byte chunk index XOR-ed by (row & 7): eight
+// consecutive rows at the same logical chunk land in eight different banks, so
+// ldmatrix reads of 8x8 blocks are conflict-free.
+template <int kRowBytes>
+__device__ __forceinline__ uint32_t swz(uint32_t row, uint32_t col) {
+    return row * kRowBytes + ((((col >> 3) ^ (row & 7u))) << 4) + (col & 7u) * 2u;
+}
+
+// (I + A)^-1 for a 64x64 strictly-lower A (fp32, row-major, stride 64): the
+// 16x16 diagonal blocks by forward substitution, then the off-diagonal blocks
+// block-diagonal by block-diagonal as T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj.
+// Only the lower triangle (j <= i) of Tm is written.  All `nthreads` threads
+// of the block must call it; it synchronizes the block internally.
+template <int nthreads>
+__device__ void solve_unit_lower(const float *A, float *Tm, float *scr) {
+    const int tid = threadIdx.x;
+    if (tid < 64) {
+        const int o = (tid >> 4) * 16, c = tid & 15;
+        float x[16];
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+            float acc = (r == c) ? 1.0f : 0.0f;
+#pragma unroll
+            for (int j = 0; j < r; ++j) acc = fmaf(-A[(o + r) * 64 + o + j], x[j], acc);
+            x[r] = acc;
+        }
+#pragma unroll
+        for (int r = 0; r < 16; ++r) Tm[(o + r) * 64 + o + c] = x[r];
+    }
+    __syncthreads();
+    for (int d = 1; d < 4; ++d) {
+        const int nblk = 4 - d;
+        for (int e = tid; e < nblk * 256; e += nthreads) {
+            const int bi = d + (e >> 8), bj = bi - d, r = (e & 255) >> 4, cc = e & 15;
+            float acc = 0.0f;
+            for (int bk = bj; bk < bi; ++bk) {
+                const float *ar = A + (16 * bi + r) * 64 + 16 * bk;
+                const float *tc = Tm + (16 * bk) * 64 + 16 * bj + cc;
+#pragma unroll
+                for (int kk = 0; kk < 16; ++kk) acc = fmaf(ar[kk], tc[kk * 64], acc);
+            }
+            scr[e] = acc;
+        }
+        __syncthreads();
+        for (int e = tid; e < nblk * 256; e += nthreads) {
+            const int bi = d + (e >> 8), bj = bi - d, r = (e & 255) >> 4, cc = e & 15;
+            const float *tr = Tm + (16 * bi + r) * 64 + 16 * bi;
+            const float *m = scr + (e & ~255) + cc;
+            float acc = 0.0f;
+#pragma unroll
+            for (int kk = 0; kk < 16; ++kk) acc = fmaf(tr[kk], m[kk * 16], acc);
+            Tm[(16 * bi + r) * 64 + 16 * bj + cc] = -acc;
+        }
+        __syncthreads();
+    }
+}
+
+}  // namespace gdn

@@ -1,16 +1,489 @@
-// gdn_prefill_chunked.cu -- chunked (C = 64) Gated DeltaNet prefill on tensor cores.
-// (placeholder: reports unsupported until the tensor-core kernel lands)
+// gdn_prefill_chunked.cu -- chunked (C = 64) Gated DeltaNet prefill on the tensor cores.
+//
+// Replaces the token-serial _gdn_prefill_kernel_v2 (solution/triton/kernel.py:138-278)
+// with the chunked WY/UT form of the same recurrence
+// (solution/gdn_baseline_torch.py:71-87).  For one (sequence, v-head) chain and a
+// chunk of tokens i, j = 0..63 with state S0 (k-last, [v][k]) at its start:
+//
+//   gamma_i = sum_{j<=i} log alpha_j,  Gamma_i = exp(gamma_i)
+//   A[i][j] = beta_i exp(gamma_i - gamma_j) k_i.k_j  (j < i),   T = (I + A)^-1
+//   R       = K S0^T                                   (the state's prediction of v)
+//   X       = diag(beta) (V - diag(Gamma) R)
+//   delta   = T X                                      (per-token innovations, [i][v])
+//   O       = scale (diag(Gamma) Q S0^T + P delta),    P[i][j] = exp(gamma_i - gamma_j) q_i.k_j (j <= i)
+//   S_end   = Gamma_63 S0 + sum_i exp(gamma_63 - gamma_i) delta_i k_i^T
+//
+// which is exactly S_t = alpha_t S_{t-1} (I - beta_t k_t k_t^T) + beta_t v_t k_t^T
+// applied token by token.  Padding tokens of a partial chunk get beta = 0 and
+// log alpha = 0 (identity rows of T, zero innovations), so K/Q/V need no masking.
+//
+// Precision: every product with an fp32 operand (S0, X, T, delta') splits that
+// operand into bf16 hi + lo (~16 significant bits), so the fp32 state tracks the
+// fp32 recurrence to ~1e-5 relative; q/k/v are exact in bf16.  Only the output
+// path (Q S0^T and P delta) uses single bf16, within the bf16 output tolerance.
+//
+// Layout: one CTA per chain, 8 warps; warp w owns state rows v = 16w..16w+15 and
+// keeps them, all 128 k columns, as fp32 mma.sync accumulators in registers for
+// the whole sequence.  The products in which v is the row index (R, Q S0^T,
+// delta, O, the state update) run per warp with no block synchronization; only
+// the chunk-wide pieces (gates, K K^T / Q K^T, the 64x64 triangular inverse) are
+// shared through swizzled shared memory.  q/k/v tiles are double-buffered with
+// cp.async.
+#include <cuda_bf16.h>
+
+#include "gdn_chunk_common.cuh"
 #include "gdn_common.cuh"
 #include "gdn_launch.h"
 
 namespace gdn {
+namespace {
 
-bool prefill_chunked_supported(const PrefillArgs &) { return false; }
+constexpr int kC = 64;
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
 
-cudaError_t launch_prefill_chunked(const PrefillArgs &, cudaStream_t) {
-    return cudaErrorNotSupported;
+// Shared memory map (bytes).
+constexpr uint32_t TILE = 64 * 256;                 // one [64][128] bf16 tile
+constexpr uint32_t OFF_K = 0;                       // 2 stages
+constexpr uint32_t OFF_Q = 2 * TILE;                // 2 stages
+constexpr uint32_t OFF_V = 4 * TILE;                // 2 stages
+constexpr uint32_t OFF_O = 6 * TILE;                // output staging [i][v]
+constexpr uint32_t OFF_P = 7 * TILE;                // [64][64] bf16
+constexpr uint32_t OFF_TH = OFF_P + 8192;           // T hi [i][j]
+constexpr uint32_t OFF_TL = OFF_TH + 8192;          // T lo
+constexpr uint32_t OFF_AF = OFF_TL + 8192;          // fp32 A [64][64]
+constexpr uint32_t OFF_TF = OFF_AF + 16384;         // fp32 T [64][64]
+constexpr uint32_t OFF_SCR = OFF_TF + 16384;        // 3 KB solve scratch
+constexpr uint32_t OFF_GATE = OFF_SCR + 3072;       // beta, gamma, Gamma, decay-to-end: 4 x 64 fp32
+constexpr uint32_t SMEM_BYTES = OFF_GATE + 1024;
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
+// 16-byte async copy global -> shared; src_bytes = 0 zero-fills the destination.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+                 "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// ldmatrix address of a 16x16 A block (rows r0.., cols c0..) of a swizzled tile.
+template <int kRowBytes>
+__device__ __forceinline__ uint32_t a_addr(uint32_t base, int r0, int c0, int lane) {
+    return base + swz<kRowBytes>(r0 + (lane & 15), c0 + ((lane >> 4) << 3));
+}
+// ldmatrix (non-trans) address for B fragments of two n-tiles (n0, n0+8) at k-step k0,
+// from a tile stored [n][k].
+template <int kRowBytes>
+__device__ __forceinline__ uint32_t b_addr_nk(uint32_t base, int n0, int k0, int lane) {
+    const int q = lane >> 3;
+    return base + swz<kRowBytes>(n0 + (lane & 7) + ((q >> 1) << 3), k0 + ((q & 1) << 3));
+}
+// ldmatrix.trans address for B fragments of two n-tiles at k-step k0, from a tile
+// stored [k][n].
+template <int kRowBytes>
+__device__ __forceinline__ uint32_t b_addr_kn(uint32_t base, int n0, int k0, int lane) {
+    const int q = lane >> 3;
+    return base + swz<kRowBytes>(k0 + (lane & 7) + ((q & 1) << 3), n0 + ((q >> 1) << 3));
+}
+
+// A fragment for k-step kk built from fp32 accumulators of n-tiles 2kk, 2kk+1
+// (the accumulator's columns become the next product's K dimension).
+__device__ __forceinline__ void acc_to_a_bf16(const float (&c0)[4], const float (&c1)[4],
+                                              uint32_t (&a)[4]) {
+    a[0] = pack_bf16x2(c0[0], c0[1]);
+    a[1] = pack_bf16x2(c0[2], c0[3]);
+    a[2] = pack_bf16x2(c1[0], c1[1]);
+    a[3] = pack_bf16x2(c1[2], c1[3]);
+}
+__device__ __forceinline__ void acc_to_a_split(const float (&c0)[4], const float (&c1)[4],
+                                               uint32_t (&hi)[4], uint32_t (&lo)[4]) {
+    float h[8], l[8];
+    const float v[8] = {c0[0], c0[1], c0[2], c0[3], c1[0], c1[1], c1[2], c1[3]};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) split_bf16(v[e], h[e], l[e]);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        hi[e] = pack_bf16x2(h[2 * e], h[2 * e + 1]);
+        lo[e] = pack_bf16x2(l[2 * e], l[2 * e + 1]);
+    }
+}
+
+struct ChunkParams {
+    const __nv_bfloat16 *q, *k, *v;
+    const float *state;
+    const void *A_log, *a, *dt_bias, *b;
+    const int32_t *cu_seqlens;
+    int64_t T;
+    int Hq, Hv;
+    float scale;
+    int gate_dtype, param_dtype;
+    __nv_bfloat16 *out;
+    float *new_state;
+};
+
+// Issue the cp.async copies of chunk tokens [t0, t0+64) into stage `st`.
+__device__ __forceinline__ void load_chunk(const ChunkParams &p, uint32_t sbase, int st,
+                                           int64_t t0, int hq, int h) {
+    const int tid = threadIdx.x;
+#pragma unroll
+    for (int u = 0; u < (64 * 16) / kThreads; ++u) {
+        const int idx = tid + u * kThreads;
+        const int j = idx >> 4, ch = idx & 15;
+        const int64_t t = t0 + j;
+        const bool ok = t < p.T;
+        const int64_t tt = ok ? t : 0;
+        const uint32_t off = j * 256 + (((ch ^ (j & 7))) << 4);
+        cp_async16(sbase + OFF_K + st * TILE + off, p.k + (tt * p.Hq + hq) * kHeadDim + ch * 8, ok ? 16 : 0);
+        cp_async16(sbase + OFF_Q + st * TILE + off, p.q + (tt * p.Hq + hq) * kHeadDim + ch * 8, ok ? 16 : 0);
+        cp_async16(sbase + OFF_V + st * TILE + off, p.v + (tt * p.Hv + h) * kHeadDim + ch * 8, ok ? 16 : 0);
+    }
+    cp_async_commit();
+}
+
+__global__ void __launch_bounds__(kThreads, 1) prefill_chunked_mma_kernel(const ChunkParams p) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t4 = lane & 3;   // mma fragment row group / column pair
+    const int64_t chain = blockIdx.x;
+    const int64_t n = chain / p.Hv;
+    const int h = static_cast<int>(chain % p.Hv);
+    const int hq = h / (p.Hv / p.Hq);
+    int64_t s0 = p.cu_seqlens[n], s1 = p.cu_seqlens[n + 1];
+    s0 = s0 < 0 ? 0 : (s0 > p.T ? p.T : s0);
+    s1 = s1 < s0 ? s0 : (s1 > p.T ? p.T : s1);
+    const int nch = static_cast<int>((s1 - s0 + kC - 1) / kC);
+    float *dst_state = p.new_state + chain * kHeadDim * kHeadDim;
+
+    if (nch == 0) {   // empty sequence: zero new state (solution/gdn_baseline_torch.py:61-62)
+        for (int i = tid; i < kHeadDim * kHeadDim / 4; i += kThreads)
+            reinterpret_cast<float4 *>(dst_state)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        return;
+    }
+
+    const uint32_t sbase = smem_u32(sm);
+    float *A_f = reinterpret_cast<float *>(sm + OFF_AF);
+    float *T_f = reinterpret_cast<float *>(sm + OFF_TF);
+    float *scr = reinterpret_cast<float *>(sm + OFF_SCR);
+    float *g_beta = reinterpret_cast<float *>(sm + OFF_GATE);
+    float *g_gam = g_beta + 64, *g_Gam = g_beta + 128, *g_dec = g_beta + 192;
+
+    // State rows v0 = 16*warp + g and v0 + 8, columns 8*nt + 2*t4 (+1): fp32 accumulators.
+    const int v0 = warp * 16 + g;
+    float S[16][4];
+    {
+        const float *src = p.state ? p.state + chain * kHeadDim * kHeadDim : nullptr;
+#pragma unroll
+        for (int nt = 0; nt < 16; ++nt) {
+            const int col = nt * 8 + 2 * t4;
+            float2 x0 = make_float2(0.f, 0.f), x1 = make_float2(0.f, 0.f);
+            if (src) {
+                x0 = *reinterpret_cast<const float2 *>(src + v0 * kHeadDim + col);
+                x1 = *reinterpret_cast<const float2 *>(src + (v0 + 8) * kHeadDim + col);
+            }
+            S[nt][0] = x0.x; S[nt][1] = x0.y; S[nt][2] = x1.x; S[nt][3] = x1.y;
+        }
+    }
+    const float exp_A = expf(load_scalar(p.A_log, h, p.param_dtype));
+    const float dtb = load_scalar(p.dt_bias, h, p.param_dtype);
+
+    load_chunk(p, sbase, 0, s0, hq, h);
+    if (nch > 1) load_chunk(p, sbase, 1, s0 + kC, hq, h);
+
+    for (int c = 0; c < nch; ++c) {
+        const int st = c & 1;
+        const int64_t t0 = s0 + static_cast<int64_t>(c) * kC;
+        const int nt_valid = static_cast<int>(s1 - t0 < kC ? s1 - t0 : kC);
+        const uint32_t sK = sbase + OFF_K + st * TILE;
+        const uint32_t sQ = sbase + OFF_Q + st * TILE;
+        const uint8_t *pV = sm + OFF_V + st * TILE;
+
+        if (c + 1 < nch) cp_async_wait<1>(); else cp_async_wait<0>();
+        // ---- gates (warp 0): beta, inclusive cumsum gamma of log alpha, Gamma, decay to chunk end
+        if (warp == 0) {
+            float lg[2], bt[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int i = lane + 32 * u;
+                lg[u] = 0.0f;
+                bt[u] = 0.0f;
+                if (i < nt_valid) {
+                    const int64_t gi = (t0 + i) * p.Hv + h;
+                    lg[u] = log_decay(exp_A, load_scalar(p.a, gi, p.gate_dtype), dtb);
+                    bt[u] = sigmoid_f(load_scalar(p.b, gi, p.gate_dtype));
+                }
+            }
+            float x0 = lg[0], x1 = lg[1];
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const float y0 = __shfl_up_sync(0xffffffffu, x0, off);
+                const float y1 = __shfl_up_sync(0xffffffffu, x1, off);
+                if (lane >= off) { x0 += y0; x1 += y1; }
+            }
+            x1 += __shfl_sync(0xffffffffu, x0, 31);
+            const float gend = __shfl_sync(0xffffffffu, x1, 31);
+            g_beta[lane] = bt[0]; g_beta[lane + 32] = bt[1];
+            g_gam[lane] = x0; g_gam[lane + 32] = x1;
+            g_Gam[lane] = expf(x0); g_Gam[lane + 32] = expf(x1);
+            g_dec[lane] = expf(gend - x0); g_dec[lane + 32] = expf(gend - x1);
+        }
+        __syncthreads();
+
+        // ---- K K^T (warps 0-3) and Q K^T (warps 4-7): rows 16*(warp&3).., all 64 columns
+        {
+            const int r0 = (warp & 3) * 16;
+            const uint32_t sA = warp < 4 ? sK : sQ;
+            float acc[8][4];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                uint32_t af[4];
+                ldsm_x4(af, a_addr<256>(sA, r0, kk * 16, lane));
+#pragma unroll
+                for (int np = 0; np < 4; ++np) {
+                    uint32_t bf[4];
+                    ldsm_x4(bf, b_addr_nk<256>(sK, np * 16, kk * 16, lane));
+                    mma16816(acc[2 * np], af, bf[0], bf[1]);
+                    mma16816(acc[2 * np + 1], af, bf[2], bf[3]);
+                }
+            }
+#pragma unroll
+            for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int i = r0 + g + ((e >> 1) << 3);
+                    const int j = nt * 8 + 2 * t4 + (e & 1);
+                    const float dec = expf(g_gam[i] - g_gam[j]);
+                    if (warp < 4) {
+                        A_f[i * 64 + j] = j < i ? g_beta[i] * dec * acc[nt][e] : 0.0f;
+                    } else {
+                        const float pv = j <= i ? dec * acc[nt][e] : 0.0f;
+                        *reinterpret_cast<__nv_bfloat16 *>(sm + OFF_P + swz<128>(i, j)) =
+                            __float2bfloat16_rn(pv);
+                    }
+                }
+        }
+        __syncthreads();
+
+        // ---- T = (I + A)^-1 (fp32), then its bf16 hi/lo parts
+        solve_unit_lower<kThreads>(A_f, T_f, scr);
+        {
+            const int i = tid >> 2, c0 = (tid & 3) * 16;
+#pragma unroll
+            for (int cc = 0; cc < 16; cc += 2) {
+                const int j = c0 + cc;
+                const float ta = j <= i ? T_f[i * 64 + j] : 0.0f;
+                const float tb = j + 1 <= i ? T_f[i * 64 + j + 1] : 0.0f;
+                float ha, la, hb, lb;
+                split_bf16(ta, ha, la);
+                split_bf16(tb, hb, lb);
+                *reinterpret_cast<uint32_t *>(sm + OFF_TH + swz<128>(i, j)) = pack_bf16x2(ha, hb);
+                *reinterpret_cast<uint32_t *>(sm + OFF_TL + swz<128>(i, j)) = pack_bf16x2(la, lb);
+            }
+        }
+        __syncthreads();
+
+        // ---- per warp: R^T = S K^T (split S), Y^T = S_hi Q^T   (rows v, columns tokens)
+        float R[8][4], Y[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) R[i][e] = Y[i][e] = 0.0f;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+            uint32_t shi[4], slo[4];
+            acc_to_a_split(S[2 * kk], S[2 * kk + 1], shi, slo);
+#pragma unroll
+            for (int np = 0; np < 4; ++np) {
+                uint32_t bk[4], bq[4];
+                ldsm_x4(bk, b_addr_nk<256>(sK, np * 16, kk * 16, lane));
+                ldsm_x4(bq, b_addr_nk<256>(sQ, np * 16, kk * 16, lane));
+                mma16816(R[2 * np], shi, bk[0], bk[1]);
+                mma16816(R[2 * np + 1], shi, bk[2], bk[3]);
+                mma16816(R[2 * np], slo, bk[0], bk[1]);
+                mma16816(R[2 * np + 1], slo, bk[2], bk[3]);
+                mma16816(Y[2 * np], shi, bq[0], bq[1]);
+                mma16816(Y[2 * np + 1], shi, bq[2], bq[3]);
+            }
+        }
+
+        // ---- X = beta (V - Gamma R), in place in R
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int j = nt * 8 + 2 * t4 + (e & 1);
+                const int v = v0 + ((e >> 1) << 3);
+                const float vv = __bfloat162float(
+                    *reinterpret_cast<const __nv_bfloat16 *>(pV + swz<256>(j, v)));
+                R[nt][e] = g_beta[j] * (vv - g_Gam[j] * R[nt][e]);
+            }
+
+        // ---- delta^T = X^T T^T (3 split products), K dimension = tokens j
+        float D[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) D[i][0] = D[i][1] = D[i][2] = D[i][3] = 0.0f;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            uint32_t xhi[4], xlo[4];
+            acc_to_a_split(R[2 * kk], R[2 * kk + 1], xhi, xlo);
+#pragma unroll
+            for (int np = 0; np < 4; ++np) {
+                uint32_t th[4], tl[4];
+                ldsm_x4(th, b_addr_nk<128>(sbase + OFF_TH, np * 16, kk * 16, lane));
+                ldsm_x4(tl, b_addr_nk<128>(sbase + OFF_TL, np * 16, kk * 16, lane));
+                mma16816(D[2 * np], xhi, th[0], th[1]);
+                mma16816(D[2 * np + 1], xhi, th[2], th[3]);
+                mma16816(D[2 * np], xlo, th[0], th[1]);
+                mma16816(D[2 * np + 1], xlo, th[2], th[3]);
+                mma16816(D[2 * np], xhi, tl[0], tl[1]);
+                mma16816(D[2 * np + 1], xhi, tl[2], tl[3]);
+            }
+        }
+
+        // ---- O^T = Gamma Y^T + delta^T P^T  (delta in bf16: output path)
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) Y[nt][e] *= g_Gam[nt * 8 + 2 * t4 + (e & 1)];
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            uint32_t da[4];
+            acc_to_a_bf16(D[2 * kk], D[2 * kk + 1], da);
+#pragma unroll
+            for (int np = 0; np < 4; ++np) {
+                uint32_t pb[4];
+                ldsm_x4(pb, b_addr_nk<128>(sbase + OFF_P, np * 16, kk * 16, lane));
+                mma16816(Y[2 * np], da, pb[0], pb[1]);
+                mma16816(Y[2 * np + 1], da, pb[2], pb[3]);
+            }
+        }
+        // stage O as [token i][v] bf16 for coalesced row stores
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int i = nt * 8 + 2 * t4 + (e & 1);
+                const int v = v0 + ((e >> 1) << 3);
+                *reinterpret_cast<__nv_bfloat16 *>(sm + OFF_O + swz<256>(i, v)) =
+                    __float2bfloat16_rn(p.scale * Y[nt][e]);
+            }
+
+        // ---- S = Gamma_63 S + (exp(gamma_63 - gamma_i) delta_i)^T K  (split delta')
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) D[i][e] *= g_dec[i * 8 + 2 * t4 + (e & 1)];
+        {
+            const float GamC = g_Gam[63];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) S[i][e] *= GamC;
+        }
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            uint32_t dhi[4], dlo[4];
+            acc_to_a_split(D[2 * kk], D[2 * kk + 1], dhi, dlo);
+#pragma unroll
+            for (int np = 0; np < 8; ++np) {
+                uint32_t bk[4];
+                ldsm_x4_t(bk, b_addr_kn<256>(sK, np * 16, kk * 16, lane));
+                mma16816(S[2 * np], dhi, bk[0], bk[1]);
+                mma16816(S[2 * np + 1], dhi, bk[2], bk[3]);
+                mma16816(S[2 * np], dlo, bk[0], bk[1]);
+                mma16816(S[2 * np + 1], dlo, bk[2], bk[3]);
+            }
+        }
+        __syncthreads();   // all warps done with stage st and the staged output
+
+        // ---- store the chunk's output rows; refill stage st with chunk c+2
+        for (int idx = tid; idx < 64 * 16; idx += kThreads) {
+            const int i = idx >> 4, ch = idx & 15;
+            if (i < nt_valid) {
+                const uint4 x = *reinterpret_cast<const uint4 *>(sm + OFF_O + i * 256 + ((ch ^ (i & 7)) << 4));
+                *reinterpret_cast<uint4 *>(p.out + ((t0 + i) * p.Hv + h) * kHeadDim + ch * 8) = x;
+            }
+        }
+        if (c + 2 < nch) load_chunk(p, sbase, st, t0 + 2 * kC, hq, h);
+    }
+
+    // Final state.
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+        const int col = nt * 8 + 2 * t4;
+        *reinterpret_cast<float2 *>(dst_state + v0 * kHeadDim + col) = make_float2(S[nt][0], S[nt][1]);
+        *reinterpret_cast<float2 *>(dst_state + (v0 + 8) * kHeadDim + col) = make_float2(S[nt][2], S[nt][3]);
+    }
+}
+
+int g_sm100_device = -2;
+
+bool device_is_sm100() {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    if (g_sm100_device == dev) return true;
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (major == 10 && minor == 0) {
+        g_sm100_device = dev;
+        return true;
+    }
+    return false;
+}
+
+}  // namespace
+
+bool prefill_chunked_supported(const PrefillArgs &p) {
+    return p.total_tokens > 0 && device_is_sm100();
+}
+
+cudaError_t launch_prefill_chunked(const PrefillArgs &p, cudaStream_t stream) {
+    const int64_t ctas = p.num_seqs * p.Hv;
+    if (ctas == 0) return cudaSuccess;
+    if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+    cudaError_t e = cudaFuncSetAttribute(prefill_chunked_mma_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    ChunkParams cp{static_cast<const __nv_bfloat16 *>(p.q), static_cast<const __nv_bfloat16 *>(p.k),
+                   static_cast<const __nv_bfloat16 *>(p.v), p.state, p.A_log, p.a, p.dt_bias, p.b,
+                   p.cu_seqlens, p.total_tokens, p.Hq, p.Hv, p.scale, p.gate_dtype, p.param_dtype,
+                   static_cast<__nv_bfloat16 *>(p.out), p.new_state};
+    prefill_chunked_mma_kernel<<<static_cast<unsigned>(ctas), kThreads, SMEM_BYTES, stream>>>(cp);
+    return cudaGetLastError();
+}
+
+// These kernels have no device-side waits, so there is never a timeout to report.
 cudaError_t read_chunked_device_error(cudaStream_t, int *code, bool) {
     *code = 0;
     return cudaSuccess;
