@@ -10,6 +10,8 @@
 //   R       = K S0^T                                   (the state's prediction of v)
 //   X       = diag(beta) (V - diag(Gamma) R)
 //   delta   = T X                                      (per-token innovations, [i][v])
+//             computed block-wise over 16-token blocks b as
+//             delta_b = T_bb (X_b - sum_{c<b} A_bc delta_c),  T_bb = (I + A_bb)^-1
 //   O       = scale (diag(Gamma) Q S0^T + P delta),    P[i][j] = exp(gamma_i - gamma_j) q_i.k_j (j <= i)
 //   S_end   = Gamma_63 S0 + sum_i exp(gamma_63 - gamma_i) delta_i k_i^T
 //
@@ -24,11 +26,12 @@
 //
 // Layout: one CTA per chain, 8 warps; warp w owns state rows v = 16w..16w+15 and
 // keeps them, all 128 k columns, as fp32 mma.sync accumulators in registers for
-// the whole sequence.  The products in which v is the row index (R, Q S0^T,
-// delta, O, the state update) run per warp with no block synchronization; only
-// the chunk-wide pieces (gates, K K^T / Q K^T, the 64x64 triangular inverse) are
-// shared through swizzled shared memory.  q/k/v tiles are double-buffered with
-// cp.async.
+// the whole sequence.  The products in which v is the row index (R, Q S0^T, the
+// blocked delta recursion, O, the state update) run per warp; only the
+// chunk-wide pieces (gates, K K^T / Q K^T and the four 16x16 diagonal inverses)
+// are shared through swizzled shared memory.  q/k/v tiles are double-buffered
+// with cp.async and the gate inputs of the next chunk are prefetched into
+// registers, so the only serial work per chunk is one 16-step substitution.
 #include <cuda_bf16.h>
 
 #include "gdn_chunk_common.cuh"
@@ -49,12 +52,11 @@ constexpr uint32_t OFF_Q = 2 * TILE;                // 2 stages
 constexpr uint32_t OFF_V = 4 * TILE;                // 2 stages
 constexpr uint32_t OFF_O = 6 * TILE;                // output staging [i][v]
 constexpr uint32_t OFF_P = 7 * TILE;                // [64][64] bf16
-constexpr uint32_t OFF_TH = OFF_P + 8192;           // T hi [i][j]
-constexpr uint32_t OFF_TL = OFF_TH + 8192;          // T lo
-constexpr uint32_t OFF_AF = OFF_TL + 8192;          // fp32 A [64][64]
-constexpr uint32_t OFF_TF = OFF_AF + 16384;         // fp32 T [64][64]
-constexpr uint32_t OFF_SCR = OFF_TF + 16384;        // 3 KB solve scratch
-constexpr uint32_t OFF_GATE = OFF_SCR + 3072;       // beta, gamma, Gamma, decay-to-end: 4 x 64 fp32
+constexpr uint32_t OFF_MH = OFF_P + 8192;           // M hi [i][j]: -A off the diagonal blocks, T_bb on them
+constexpr uint32_t OFF_ML = OFF_MH + 8192;          // M lo
+constexpr uint32_t OFF_AD = OFF_ML + 8192;          // fp32 diagonal blocks of A: 4 x [16][17]
+constexpr uint32_t AD_STRIDE = 17;
+constexpr uint32_t OFF_GATE = OFF_AD + 4 * 16 * AD_STRIDE * 4;   // beta, gamma, Gamma, decay-to-end
 constexpr uint32_t SMEM_BYTES = OFF_GATE + 1024;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -190,9 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_chunked_mma_kernel(const 
     }
 
     const uint32_t sbase = smem_u32(sm);
-    float *A_f = reinterpret_cast<float *>(sm + OFF_AF);
-    float *T_f = reinterpret_cast<float *>(sm + OFF_TF);
-    float *scr = reinterpret_cast<float *>(sm + OFF_SCR);
+    float *A_d = reinterpret_cast<float *>(sm + OFF_AD);
     float *g_beta = reinterpret_cast<float *>(sm + OFF_GATE);
     float *g_gam = g_beta + 64, *g_Gam = g_beta + 128, *g_dec = g_beta + 192;
 
@@ -218,6 +218,21 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_chunked_mma_kernel(const 
     load_chunk(p, sbase, 0, s0, hq, h);
     if (nch > 1) load_chunk(p, sbase, 1, s0 + kC, hq, h);
 
+    // Warp 0 keeps the next chunk's raw gate inputs in registers (loaded one chunk ahead).
+    float ga[2] = {0.f, 0.f}, gb[2] = {0.f, 0.f};
+    auto fetch_gates = [&](int64_t tbase, int nvalid) {
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int i = lane + 32 * u;
+            if (i < nvalid) {
+                const int64_t gi = (tbase + i) * p.Hv + h;
+                ga[u] = load_scalar(p.a, gi, p.gate_dtype);
+                gb[u] = load_scalar(p.b, gi, p.gate_dtype);
+            }
+        }
+    };
+    if (warp == 0) fetch_gates(s0, static_cast<int>(s1 - s0 < kC ? s1 - s0 : kC));
+
     for (int c = 0; c < nch; ++c) {
         const int st = c & 1;
         const int64_t t0 = s0 + static_cast<int64_t>(c) * kC;
@@ -236,10 +251,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_chunked_mma_kernel(const 
                 lg[u] = 0.0f;
                 bt[u] = 0.0f;
                 if (i < nt_valid) {
-                    const int64_t gi = (t0 + i) * p.Hv + h;
-                    lg[u] = log_decay(exp_A, load_scalar(p.a, gi, p.gate_dtype), dtb);
-                    bt[u] = sigmoid_f(load_scalar(p.b, gi, p.gate_dtype));
+                    lg[u] = log_decay(exp_A, ga[u], dtb);
+                    bt[u] = sigmoid_f(gb[u]);
                 }
+            }
+            if (c + 1 < nch) {
+                const int64_t tn = t0 + kC;
+                fetch_gates(tn, static_cast<int>(s1 - tn < kC ? s1 - tn : kC));
             }
             float x0 = lg[0], x1 = lg[1];
 #pragma unroll
@@ -276,41 +294,72 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_chunked_mma_kernel(const 
                     mma16816(acc[2 * np + 1], af, bf[2], bf[3]);
                 }
             }
+            // Epilogue.  Warps 0-3 (K K^T, row block w): the diagonal block of A in fp32
+            // for the 16x16 inverse, -A as bf16 hi/lo on the blocks left of it, zeros
+            // to its right.  Warps 4-7 (Q K^T): P in bf16.
+            const int blk = warp & 3;
 #pragma unroll
-            for (int nt = 0; nt < 8; ++nt)
+            for (int nt = 0; nt < 8; ++nt) {
+                const int j0 = nt * 8 + 2 * t4;
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int i = r0 + g + ((e >> 1) << 3);
-                    const int j = nt * 8 + 2 * t4 + (e & 1);
-                    const float dec = expf(g_gam[i] - g_gam[j]);
+                for (int half = 0; half < 2; ++half) {
+                    const int i = r0 + g + half * 8;
+                    const float gi = g_gam[i];
+                    float vals[2];
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const int j = j0 + u;
+                        const float dec = j <= i ? expf(gi - g_gam[j]) : 0.0f;
+                        vals[u] = dec * acc[nt][2 * half + u];
+                    }
                     if (warp < 4) {
-                        A_f[i * 64 + j] = j < i ? g_beta[i] * dec * acc[nt][e] : 0.0f;
+                        const int jb = nt >> 1;   // column block of j0, j0+1
+                        if (jb == blk) {
+#pragma unroll
+                            for (int u = 0; u < 2; ++u) {
+                                const int j = j0 + u;
+                                A_d[(blk * 16 + (i & 15)) * AD_STRIDE + (j & 15)] =
+                                    j < i ? g_beta[i] * vals[u] : 0.0f;
+                            }
+                        } else {
+                            float h0 = 0.f, l0 = 0.f, h1 = 0.f, l1 = 0.f;
+                            if (jb < blk) {
+                                split_bf16(-g_beta[i] * vals[0], h0, l0);
+                                split_bf16(-g_beta[i] * vals[1], h1, l1);
+                            }
+                            *reinterpret_cast<uint32_t *>(sm + OFF_MH + swz<128>(i, j0)) = pack_bf16x2(h0, h1);
+                            *reinterpret_cast<uint32_t *>(sm + OFF_ML + swz<128>(i, j0)) = pack_bf16x2(l0, l1);
+                        }
                     } else {
-                        const float pv = j <= i ? dec * acc[nt][e] : 0.0f;
-                        *reinterpret_cast<__nv_bfloat16 *>(sm + OFF_P + swz<128>(i, j)) =
-                            __float2bfloat16_rn(pv);
+                        *reinterpret_cast<uint32_t *>(sm + OFF_P + swz<128>(i, j0)) = pack_bf16x2(vals[0], vals[1]);
                     }
                 }
-        }
-        __syncthreads();
-
-        // ---- T = (I + A)^-1 (fp32), then its bf16 hi/lo parts
-        solve_unit_lower<kThreads>(A_f, T_f, scr);
-        {
-            const int i = tid >> 2, c0 = (tid & 3) * 16;
-#pragma unroll
-            for (int cc = 0; cc < 16; cc += 2) {
-                const int j = c0 + cc;
-                const float ta = j <= i ? T_f[i * 64 + j] : 0.0f;
-                const float tb = j + 1 <= i ? T_f[i * 64 + j + 1] : 0.0f;
-                float ha, la, hb, lb;
-                split_bf16(ta, ha, la);
-                split_bf16(tb, hb, lb);
-                *reinterpret_cast<uint32_t *>(sm + OFF_TH + swz<128>(i, j)) = pack_bf16x2(ha, hb);
-                *reinterpret_cast<uint32_t *>(sm + OFF_TL + swz<128>(i, j)) = pack_bf16x2(la, lb);
             }
         }
         __syncthreads();
+
+        // ---- T_bb = (I + A_bb)^-1 for the four 16x16 diagonal blocks (threads 0-63,
+        //      one column each, forward substitution in fp32) -> bf16 hi/lo into M
+        if (tid < 64) {
+            const int b = tid >> 4, col = tid & 15;
+            const float *Ab = A_d + b * 16 * AD_STRIDE;
+            float x[16];
+#pragma unroll
+            for (int r = 0; r < 16; ++r) {
+                float acc = (r == col) ? 1.0f : 0.0f;
+#pragma unroll
+                for (int j = 0; j < r; ++j) acc = fmaf(-Ab[r * AD_STRIDE + j], x[j], acc);
+                x[r] = acc;
+            }
+#pragma unroll
+            for (int r = 0; r < 16; ++r) {
+                float hx, lx;
+                split_bf16(x[r], hx, lx);
+                const uint32_t off = swz<128>(b * 16 + r, b * 16 + col);
+                *reinterpret_cast<__nv_bfloat16 *>(sm + OFF_MH + off) = __float2bfloat16_rn(hx);
+                *reinterpret_cast<__nv_bfloat16 *>(sm + OFF_ML + off) = __float2bfloat16_rn(lx);
+            }
+        }
 
         // ---- per warp: R^T = S K^T (split S), Y^T = S_hi Q^T   (rows v, columns tokens)
         float R[8][4], Y[8][4];
@@ -348,26 +397,40 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_chunked_mma_kernel(const 
                 R[nt][e] = g_beta[j] * (vv - g_Gam[j] * R[nt][e]);
             }
 
-        // ---- delta^T = X^T T^T (3 split products), K dimension = tokens j
+        __syncthreads();   // M (diagonal inverses) and P are complete
+
+        // ---- delta^T block by block: delta_b^T = (X_b^T - sum_{c<b} delta_c^T A_bc^T) T_bb^T
         float D[8][4];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) D[i][0] = D[i][1] = D[i][2] = D[i][3] = 0.0f;
+        for (int bb = 0; bb < 4; ++bb) {
+            float Z[2][4];
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-            uint32_t xhi[4], xlo[4];
-            acc_to_a_split(R[2 * kk], R[2 * kk + 1], xhi, xlo);
+            for (int e = 0; e < 4; ++e) { Z[0][e] = R[2 * bb][e]; Z[1][e] = R[2 * bb + 1][e]; }
 #pragma unroll
-            for (int np = 0; np < 4; ++np) {
-                uint32_t th[4], tl[4];
-                ldsm_x4(th, b_addr_nk<128>(sbase + OFF_TH, np * 16, kk * 16, lane));
-                ldsm_x4(tl, b_addr_nk<128>(sbase + OFF_TL, np * 16, kk * 16, lane));
-                mma16816(D[2 * np], xhi, th[0], th[1]);
-                mma16816(D[2 * np + 1], xhi, th[2], th[3]);
-                mma16816(D[2 * np], xlo, th[0], th[1]);
-                mma16816(D[2 * np + 1], xlo, th[2], th[3]);
-                mma16816(D[2 * np], xhi, tl[0], tl[1]);
-                mma16816(D[2 * np + 1], xhi, tl[2], tl[3]);
+            for (int cc = 0; cc < bb; ++cc) {
+                uint32_t dhi[4], dlo[4], mh[4], ml[4];
+                acc_to_a_split(D[2 * cc], D[2 * cc + 1], dhi, dlo);
+                ldsm_x4(mh, b_addr_nk<128>(sbase + OFF_MH, bb * 16, cc * 16, lane));
+                ldsm_x4(ml, b_addr_nk<128>(sbase + OFF_ML, bb * 16, cc * 16, lane));
+                mma16816(Z[0], dhi, mh[0], mh[1]);
+                mma16816(Z[1], dhi, mh[2], mh[3]);
+                mma16816(Z[0], dlo, mh[0], mh[1]);
+                mma16816(Z[1], dlo, mh[2], mh[3]);
+                mma16816(Z[0], dhi, ml[0], ml[1]);
+                mma16816(Z[1], dhi, ml[2], ml[3]);
             }
+            uint32_t zhi[4], zlo[4], th[4], tl[4];
+            acc_to_a_split(Z[0], Z[1], zhi, zlo);
+            ldsm_x4(th, b_addr_nk<128>(sbase + OFF_MH, bb * 16, bb * 16, lane));
+            ldsm_x4(tl, b_addr_nk<128>(sbase + OFF_ML, bb * 16, bb * 16, lane));
+#pragma unroll
+            for (int e = 0; e < 4; ++e) D[2 * bb][e] = D[2 * bb + 1][e] = 0.0f;
+            mma16816(D[2 * bb], zhi, th[0], th[1]);
+            mma16816(D[2 * bb + 1], zhi, th[2], th[3]);
+            mma16816(D[2 * bb], zlo, th[0], th[1]);
+            mma16816(D[2 * bb + 1], zlo, th[2], th[3]);
+            mma16816(D[2 * bb], zhi, tl[0], tl[1]);
+            mma16816(D[2 * bb + 1], zhi, tl[2], tl[3]);
         }
 
         // ---- O^T = Gamma Y^T + delta^T P^T  (delta in bf16: output path)
