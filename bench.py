@@ -54,6 +54,20 @@ def load_peaks():
         return dict(FALLBACK_PEAKS, source="fallback")
 
 
+def profiled_traffic(name):
+    """DRAM bytes per unit of work from a committed ncu summary (profiles/<name>.md,
+    line 'dram_bytes_per_unit: <float>'), or None."""
+    path = os.path.join(REPO, "profiles", name + ".md")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.strip().startswith("dram_bytes_per_unit:"):
+                    return float(line.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
 def dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -74,23 +88,31 @@ def base_config(n_gpus):
             "parallelism": f"replicas{n_gpus} (sequence/head sharding, no collective)"}
 
 
-def cpu_prefill_sample(impl, budget_s, threads):
-    """Time a CPU implementation on the first tokens of one 8192-token sequence
-    (all 32 heads, nonzero state), growing the sample until ~budget_s of work."""
+def cpu_prefill_sample(impl, budget_s):
+    """Time a CPU implementation on a prefix of the 16 x 8192 workload (all 32
+    heads, nonzero state), growing the sample until it takes ~budget_s."""
     from fastaf_kernel_b200 import workloads as W
-    x = W.prefill_inputs([SEQ_LEN], seed=3, decay_range=(0.5, 0.999))
-    n = 32
+    x = W.prefill_long(seed=3)
+    n = 256
+    total = N_SEQS * SEQ_LEN
     while True:
-        cu = torch.tensor([0, n], dtype=torch.int32)
-        sl = lambda t: t[:n]
-        args = (sl(x["q"]), sl(x["k"]), sl(x["v"]), x["state"], x["A_log"], sl(x["a"]),
-                x["dt_bias"], sl(x["b"]), cu, x["scale"])
+        lens = []
+        left = n
+        while left > 0:
+            lens.append(min(SEQ_LEN, left))
+            left -= lens[-1]
+        cu = torch.zeros(len(lens) + 1, dtype=torch.int32)
+        cu[1:] = torch.cumsum(torch.tensor(lens), 0)
+        idx = torch.cat([torch.arange(s * SEQ_LEN, s * SEQ_LEN + L) for s, L in enumerate(lens)])
+        sl = lambda t: t.index_select(0, idx)
+        args = (sl(x["q"]), sl(x["k"]), sl(x["v"]), x["state"][:len(lens)], x["A_log"],
+                sl(x["a"]), x["dt_bias"], sl(x["b"]), cu, x["scale"])
         t0 = time.perf_counter()
         impl(*args)
         dt = time.perf_counter() - t0
-        if dt >= budget_s or n >= SEQ_LEN:
-            return n / dt, n, dt
-        n = min(SEQ_LEN, max(n * 2, int(n * budget_s / max(dt, 1e-3) * 1.1)))
+        if dt >= budget_s or n >= total:
+            return n / dt, n, len(lens), dt
+        n = min(total, max(n * 2, int(n * budget_s / max(dt, 1e-3) * 1.1)))
 
 
 def reference_arm(args):
@@ -148,7 +170,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--method", choices=["auto", "chunked", "recurrent"], default="auto")
-    ap.add_argument("--cpu-budget", type=float, default=10.0,
+    ap.add_argument("--cpu-budget", type=float, default=12.0,
                     help="seconds of CPU work for the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -204,12 +226,12 @@ def main():
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
-        evs[0].record(stream)
-        for i in range(args.steps):
-            prefill_step()
-            evs[i + 1].record(stream)
-        torch.cuda.synchronize()
+    clk = ClockSampler(local, period_ms=50).__enter__()
+    evs[0].record(stream)
+    for i in range(args.steps):
+        prefill_step()
+        evs[i + 1].record(stream)
+    torch.cuda.synchronize()
     barrier()
     launch_ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
     total_ms = max_over_ranks(evs[0].elapsed_time(evs[-1]))
@@ -221,7 +243,9 @@ def main():
     pbytes = W.prefill_bytes(T, N_SEQS, N_SEQS)
     roofline = {"bound": "tensor", "achieved": achieved_tflops, "peak": peaks["bf16_tflops"],
                 "unit": "TFLOP/s", "frac": achieved_tflops / peaks["bf16_tflops"],
-                "traffic": None, "peak_source": peaks["source"],
+                "traffic": (lambda b: None if b is None else b * T)(
+                    profiled_traffic("ncu_prefill_chunked_16x4096")),
+                "peak_source": peaks["source"],
                 "kernel": "gdn prefill (" + args.method + ")",
                 "flops_per_launch": flops, "algorithmic_bytes_per_launch": pbytes,
                 "hbm_gbs_achieved": pbytes / avg_launch_s / 1e9,
@@ -260,7 +284,9 @@ def main():
               "steps": DECODE_STEPS,
               "roofline": {"bound": "hbm", "achieved": dec_gbs, "peak": peaks["hbm_gbs"],
                            "unit": "GB/s", "frac": dec_gbs / peaks["hbm_gbs"],
-                           "traffic": None, "peak_source": peaks["source"],
+                           "traffic": (lambda b: None if b is None else b * DECODE_B)(
+                               profiled_traffic("ncu_decode_b512")),
+                           "peak_source": peaks["source"],
                            "bytes_per_launch": dec_bytes}}
 
     # ---------------- end to end through the public API, host buffers ----------------
@@ -302,17 +328,19 @@ def main():
                "path": "pinned host -> device copies, fastaf_kernel_b200.kernel, device -> "
                        "pinned host copies of output and new_state"}
 
+    clk.__exit__(None, None, None)
+
     # ---------------- CPU baseline (rank 0, one GPU only) ----------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         from oracle import c_oracle
         threads = os.cpu_count() or 1
-        tps, n_tok, dt = cpu_prefill_sample(
-            lambda *a: c_oracle.prefill(*a, num_threads=threads), args.cpu_budget, threads)
+        tps, n_tok, n_seq, dt = cpu_prefill_sample(
+            lambda *a: c_oracle.prefill(*a, num_threads=threads), args.cpu_budget)
         cpu = {"value": tps, "unit": UNIT, "cores": threads, "kind": "port",
-               "impl": "oracle/gdn_oracle.c (fp32 recurrence, OpenMP over v-heads)",
-               "sample": f"first {n_tok} tokens of one {SEQ_LEN}-token sequence, 32 v-heads, "
-                         f"nonzero state ({dt:.1f} s)"}
+               "impl": "oracle/gdn_oracle.c (fp32 recurrence, OpenMP over (sequence, v-head))",
+               "sample": f"first {n_tok} tokens ({n_seq} sequences) of the {N_SEQS}x{SEQ_LEN} "
+                         f"workload, 32 v-heads, nonzero state ({dt:.1f} s)"}
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
