@@ -25,6 +25,7 @@ GDN_DTYPE_BF16 = 1
 GDN_PREFILL_AUTO = 0
 GDN_PREFILL_CHUNKED = 1
 GDN_PREFILL_RECURRENT = 2
+GDN_PREFILL_TCGEN05 = 3
 
 # Every symbol include/gdn_b200.h declares.
 EXPORTED_SYMBOLS = ("gdn_prefill", "gdn_prefill_ex", "gdn_decode", "gdn_device_status",

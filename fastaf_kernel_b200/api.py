@@ -27,7 +27,7 @@ __all__ = ["kernel", "kernel_decode", "kernel_dps", "kernel_decode_dps", "device
 
 _GATE_DTYPES = {torch.float32: _lib.GDN_DTYPE_F32, torch.bfloat16: _lib.GDN_DTYPE_BF16}
 _METHODS = {"auto": _lib.GDN_PREFILL_AUTO, "chunked": _lib.GDN_PREFILL_CHUNKED,
-            "recurrent": _lib.GDN_PREFILL_RECURRENT}
+            "recurrent": _lib.GDN_PREFILL_RECURRENT, "tcgen05": _lib.GDN_PREFILL_TCGEN05}
 
 
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:

@@ -66,12 +66,8 @@ const char *gdn_version(void) { return "gdn_b200 0.1.0 sm_100a"; }
 int gdn_device_status(void *stream) {
     g_last_error[0] = '\0';
     int code = 0;
-    const cudaError_t e = gdn::read_chunked_device_error(static_cast<cudaStream_t>(stream), &code, true);
+    const cudaError_t e = gdn::read_tc_device_error(static_cast<cudaStream_t>(stream), &code, true);
     if (e != cudaSuccess) return cuda_status(e, "gdn_device_status");
-    int rec[4] = {0, 0, 0, 0};
-    if (gdn::read_chunked_check_record(static_cast<cudaStream_t>(stream), rec) == cudaSuccess && rec[3] != 0)
-        return fail(GDN_ERR_DEVICE_TIMEOUT, "address check failed at site %d value %lld (%d failures)",
-                    rec[0], (long long)(((int64_t)rec[2] << 32) | (uint32_t)rec[1]), rec[3]);
     if (code != 0)
         return fail(GDN_ERR_DEVICE_TIMEOUT, "a prefill CTA timed out waiting at site %d", code);
     return GDN_OK;
@@ -122,7 +118,8 @@ int gdn_prefill_ex(const void *q, const void *k, const void *v, const float *sta
         if (ranges_overlap(state, state_bytes, new_state, state_bytes))
             return fail(GDN_ERR_INVALID_ARGUMENT, "prefill new_state must not overlap state");
     }
-    if (method != GDN_PREFILL_AUTO && method != GDN_PREFILL_CHUNKED && method != GDN_PREFILL_RECURRENT)
+    if (method != GDN_PREFILL_AUTO && method != GDN_PREFILL_CHUNKED && method != GDN_PREFILL_RECURRENT &&
+        method != GDN_PREFILL_TCGEN05)
         return fail(GDN_ERR_INVALID_ARGUMENT, "unknown prefill method %d", method);
     if (num_seqs == 0) return GDN_OK;
     gdn::PrefillArgs p{q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs, total_tokens,
@@ -130,6 +127,12 @@ int gdn_prefill_ex(const void *q, const void *k, const void *v, const float *sta
                        scale == 0.0f ? 1.0f / sqrtf(static_cast<float>(head_size)) : scale,
                        gate_dtype, param_dtype, output, new_state};
     const auto s = static_cast<cudaStream_t>(stream);
+    if (method == GDN_PREFILL_TCGEN05) {
+        if (!gdn::prefill_tc_supported(p))
+            return fail(GDN_ERR_UNSUPPORTED,
+                        "the tcgen05 prefill needs an sm_100 device and total_tokens >= 64");
+        return cuda_status(gdn::launch_prefill_tc(p, s), "gdn_prefill (tcgen05) launch");
+    }
     const bool chunked_ok = gdn::prefill_chunked_supported(p);
     if (method == GDN_PREFILL_CHUNKED && !chunked_ok)
         return fail(GDN_ERR_UNSUPPORTED, "the chunked tensor-core prefill is not available here");

@@ -36,7 +36,9 @@ cudaError_t launch_decode(const DecodeArgs &p, cudaStream_t stream);
 cudaError_t launch_prefill_recurrent(const PrefillArgs &p, cudaStream_t stream);
 cudaError_t launch_prefill_chunked(const PrefillArgs &p, cudaStream_t stream);
 bool prefill_chunked_supported(const PrefillArgs &p);
-cudaError_t read_chunked_device_error(cudaStream_t stream, int *code, bool clear);
-cudaError_t read_chunked_check_record(cudaStream_t stream, int rec[4]);
+cudaError_t launch_prefill_tc(const PrefillArgs &p, cudaStream_t stream);
+bool prefill_tc_supported(const PrefillArgs &p);
+// Site of the first bounded device wait of the tcgen05 prefill that gave up (0 = none).
+cudaError_t read_tc_device_error(cudaStream_t stream, int *code, bool clear);
 
 }  // namespace gdn

@@ -546,15 +546,4 @@ cudaError_t launch_prefill_chunked(const PrefillArgs &p, cudaStream_t stream) {
     return cudaGetLastError();
 }
 
-// These kernels have no device-side waits, so there is never a timeout to report.
-cudaError_t read_chunked_device_error(cudaStream_t, int *code, bool) {
-    *code = 0;
-    return cudaSuccess;
-}
-
-cudaError_t read_chunked_check_record(cudaStream_t, int rec[4]) {
-    rec[0] = rec[1] = rec[2] = rec[3] = 0;
-    return cudaSuccess;
-}
-
 }  // namespace gdn

@@ -164,6 +164,90 @@ selftest_kernel(const __grid_constant__ CUtensorMap xmap, int mode, const __nv_b
     if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
+
+// Warp-role layout check (256 threads): warp 0 allocates all 512 TMEM columns and
+// its lane 0 issues the MMAs (the allocating warp is the issuing warp); warps 4-7
+// write the A operand into TMEM with 32-column stores and read the accumulator
+// back with 32-column loads.  D = A[128][K] * B[N][K]^T with A in TMEM at column
+// a_col and D at column d_col; B K-major in shared memory.
+__global__ void __launch_bounds__(256, 1)
+selftest_roles_kernel(const __nv_bfloat16 *A, const __nv_bfloat16 *B, int N, int K, int a_col,
+                      int d_col, float *D, int *status) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint64_t bar;
+    __shared__ uint32_t tmem_slot;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint32_t b_mma = smem_u32(&bar);
+    if (warp == 0) {
+        if (lane == 0) {
+            mbar_init(b_mma, 1);
+            fence_mbar_init();
+        }
+        __syncwarp();
+        tmem_alloc(smem_u32(&tmem_slot), 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    uint8_t *sB = smem + kSmemB;
+    // B by all threads; A into TMEM by warps 4-7 (thread m = row m).
+    for (int idx = threadIdx.x; idx < N * (K / 8); idx += blockDim.x) {
+        const int r = idx / (K / 8), c8 = idx % (K / 8);
+        *reinterpret_cast<uint4 *>(sB + (c8 / 8) * (N * 128) + sw128(r, c8 % 8)) =
+            *reinterpret_cast<const uint4 *>(B + r * K + c8 * 8);
+    }
+    if (warp >= 4) {
+        const int m = (warp - 4) * 32 + lane;
+        const uint32_t *row = reinterpret_cast<const uint32_t *>(A + m * K);
+        for (int c0 = 0; c0 < K / 2; c0 += 32) {
+            uint32_t r[32];
+            for (int j = 0; j < 32; ++j) r[j] = row[c0 + j];
+            tmem_st32(tmem_addr(tmem, (warp & 3) * 32, a_col + c0), r);
+        }
+        tmem_wait_st();
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    bool ok = true;
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint32_t idesc = idesc_bf16_f32(128, N, false, false);
+            const uint32_t b0 = smem_u32(sB);
+            for (int s = 0; s < K / 16; ++s)
+                mma_ts(tmem + d_col, tmem + a_col + s * 8,
+                       smem_desc_sw128(b0 + (s / 4) * (N * 128) + (s % 4) * 32, 16, 1024), idesc,
+                       s > 0);
+            mma_commit(b_mma);
+        }
+        __syncwarp();
+    }
+    ok = mbar_wait(b_mma, 0);
+    tc_fence_after();
+    if (ok && warp >= 4) {
+        const int m = (warp - 4) * 32 + lane;
+        for (int c0 = 0; c0 < N; c0 += 32) {
+            uint32_t r[32];
+            tmem_ld32(tmem_addr(tmem, (warp & 3) * 32, d_col + c0), r);
+            tmem_wait_ld_dep(r);
+            for (int j = 0; j < 32; ++j) D[m * N + c0 + j] = __uint_as_float(r[j]);
+        }
+    }
+    if (!ok && threadIdx.x == 0) atomicExch(status, 1);
+    if (!ok) mbar_wait(b_mma, 0);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
 }  // namespace
 }  // namespace gdn
 
@@ -186,5 +270,25 @@ extern "C" __attribute__((visibility("default"))) int gdn_selftest_umma(
     selftest_kernel<<<1, 128, kSmemBytes + 1024, s>>>(
         map, mode, static_cast<const __nv_bfloat16 *>(A), static_cast<const __nv_bfloat16 *>(B), h,
         N, K, D, status);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+// Warp-role layout check; a_col, d_col are TMEM column offsets (A needs K/2 columns,
+// D needs N columns, both inside the 512 allocated).
+extern "C" __attribute__((visibility("default"))) int gdn_selftest_roles(
+    const void *A, const void *B, int N, int K, int a_col, int d_col, float *D, int *status,
+    void *stream) {
+    using namespace gdn;
+    if ((N != 64 && N != 128) || (K != 64 && K != 128)) return -1;
+    if (a_col < 0 || a_col % 32 || a_col + K / 2 > 512) return -1;
+    if (d_col < 0 || d_col % 32 || d_col + N > 512) return -1;
+    if ((a_col < d_col + N) && (d_col < a_col + K / 2)) return -1;   // must not overlap
+    cudaError_t e = cudaFuncSetAttribute(selftest_roles_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kSmemBytes + 1024);
+    if (e != cudaSuccess) return -3;
+    selftest_roles_kernel<<<1, 256, kSmemBytes + 1024, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const __nv_bfloat16 *>(A), static_cast<const __nv_bfloat16 *>(B), N, K, a_col,
+        d_col, D, status);
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }

@@ -44,8 +44,9 @@ extern "C" {
 
 /* Prefill kernel choice for gdn_prefill_ex(). */
 #define GDN_PREFILL_AUTO 0      /* chunked tensor-core kernel when supported */
-#define GDN_PREFILL_CHUNKED 1   /* chunked (C=64) WY/UT kernel on tcgen05 tensor cores */
+#define GDN_PREFILL_CHUNKED 1   /* chunked (C=64) WY/UT kernel on the tensor cores (mma.sync) */
 #define GDN_PREFILL_RECURRENT 2 /* token-serial CUDA-core kernel */
+#define GDN_PREFILL_TCGEN05 3   /* chunked (C=64) kernel on tcgen05 + TMEM + TMA; T >= 64 */
 
 /*
  * Varlen chunked prefill.

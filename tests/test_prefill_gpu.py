@@ -1,7 +1,7 @@
 """Prefill kernels on the GPU against the CPU oracle (through the C ABI).
 
-Both prefill kernels are covered: the chunked (C=64) tensor-core kernel and the
-token-serial CUDA-core kernel."""
+All three prefill kernels are covered: the chunked (C=64) kernel on tcgen05 +
+TMEM + TMA, the chunked kernel on mma.sync, and the token-serial CUDA-core kernel."""
 import numpy as np
 import pytest
 import torch
@@ -14,7 +14,8 @@ from tolerances import assert_parity
 
 pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda", 0)
-METHODS = ["chunked", "recurrent"]
+METHODS = ["tcgen05", "chunked", "recurrent"]
+TC_MIN_TOKENS = 64   # the tcgen05 kernel's TMA box is 64 tokens deep
 
 
 def _gpu(d):
@@ -23,6 +24,12 @@ def _gpu(d):
 
 def _prefill(x, method, **kw):
     g = _gpu(x)
+    if method == "tcgen05" and g["q"].shape[0] < TC_MIN_TOKENS:
+        # Refused before any launch, with the library's "unsupported" status.
+        with pytest.raises(NotImplementedError):
+            fk.kernel(g["q"], g["k"], g["v"], g["state"], g["A_log"], g["a"], g["dt_bias"],
+                      g["b"], g["cu_seqlens"], g["scale"], method=method, **kw)
+        pytest.skip("the tcgen05 kernel needs at least 64 packed tokens")
     o, s = fk.kernel(g["q"], g["k"], g["v"], g["state"], g["A_log"], g["a"], g["dt_bias"],
                      g["b"], g["cu_seqlens"], g["scale"], method=method, **kw)
     fk.device_status()   # synchronizes; raises if a bounded device wait timed out
@@ -122,14 +129,15 @@ def test_prefill_gva_ratios(method):
 
 
 def test_chunked_equals_recurrent_long_prefill_sample():
-    """Full-size long-prefill shapes (16 x 8192, 32 heads): the two independent CUDA
+    """Full-size long-prefill shapes (16 x 8192, 32 heads): the three independent CUDA
     kernels agree; the oracle checks sequence 0 over its first 2048 tokens."""
     x = W.prefill_long(seed=3, device=DEV)
     outs = {}
     for m in METHODS:
         outs[m] = _prefill(x, m)
-    (oc, sc), (orr, sr) = outs["chunked"], outs["recurrent"]
+    (oc, sc), (orr, sr), (ot, st) = outs["chunked"], outs["recurrent"], outs["tcgen05"]
     assert_parity(oc, orr, sc, sr)
+    assert_parity(ot, orr, st, sr)
     n = 2048
     sub = {k: (v[:n].cpu() if isinstance(v, torch.Tensor) and v.shape[0] == 16 * 8192 else v)
            for k, v in x.items()}
@@ -137,8 +145,9 @@ def test_chunked_equals_recurrent_long_prefill_sample():
     sub["cu_seqlens"] = torch.tensor([0, n], dtype=torch.int32)
     sub["A_log"], sub["dt_bias"] = x["A_log"].cpu(), x["dt_bias"].cpu()
     ro, rs = _oracle(sub)
-    o2, s2 = _prefill(sub, "chunked")
-    assert_parity(o2.cpu(), ro, s2.cpu(), rs)
+    for m in ("chunked", "tcgen05"):
+        o2, s2 = _prefill(sub, m)
+        assert_parity(o2.cpu(), ro, s2.cpu(), rs)
 
 
 @pytest.mark.parametrize("method", METHODS)

@@ -76,3 +76,31 @@ def test_tma_mnmajor_b_with_tmem_a():
     Bm = X[64:, 0, :].double().T                     # B[d][t] = X[64+t][h][d]
     ref = A.double() @ Bm.T
     assert torch.allclose(D, ref, rtol=1e-5, atol=1e-4), (D - ref).abs().max()
+
+
+def _roles_lib():
+    lib = ctypes.CDLL(SELFTEST_LIB_PATH)
+    vp, i32 = ctypes.c_void_p, ctypes.c_int
+    lib.gdn_selftest_roles.argtypes = [vp, vp, i32, i32, i32, i32, vp, vp, vp]
+    lib.gdn_selftest_roles.restype = i32
+    return lib
+
+
+@pytest.mark.parametrize("N,K,a_col,d_col", [(64, 128, 192, 448), (128, 64, 0, 256),
+                                             (64, 64, 384, 256), (128, 128, 320, 128)])
+def test_warp_roles_full_tmem(N, K, a_col, d_col):
+    """All 512 TMEM columns allocated by warp 0, MMAs issued by warp 0, the
+    accumulator at a nonzero column, 32-column TMEM stores/loads by warps 4-7."""
+    g = torch.Generator().manual_seed(N * 7 + K + a_col + d_col)
+    A, B = _rand((128, K), g), _rand((N, K), g)
+    D = torch.full((128, N), float("nan"), device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    Ad, Bd = A.to(DEV), B.to(DEV)   # keep the device copies alive across the launch
+    rc = _roles_lib().gdn_selftest_roles(Ad.data_ptr(), Bd.data_ptr(), N, K, a_col, d_col,
+                                         D.data_ptr(), status.data_ptr(),
+                                         torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    ref = A.double() @ B.double().T
+    assert torch.allclose(D.cpu().double(), ref, rtol=1e-5, atol=1e-4)
