@@ -169,7 +169,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--method", choices=["auto", "chunked", "recurrent"], default="auto")
+    ap.add_argument("--method", choices=["auto", "tcgen05", "chunked", "recurrent"], default="auto")
     ap.add_argument("--cpu-budget", type=float, default=12.0,
                     help="seconds of CPU work for the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
@@ -211,6 +211,9 @@ def main():
     # ---------------- prefill: inputs resident in HBM ----------------
     x = W.prefill_long(seed=3 + rank, device=dev)
     T = N_SEQS * SEQ_LEN
+    kernel_name = fk.prefill_method(T, args.method)
+    # the tcgen05 path is two launches per step (chunk prep, then the chains)
+    launches_per_step = 2 if kernel_name == "tcgen05" else 1
     out = torch.empty((T, 32, 128), dtype=torch.bfloat16, device=dev)
     ns = torch.empty((N_SEQS, 32, 128, 128), dtype=torch.float32, device=dev)
 
@@ -244,9 +247,9 @@ def main():
     roofline = {"bound": "tensor", "achieved": achieved_tflops, "peak": peaks["bf16_tflops"],
                 "unit": "TFLOP/s", "frac": achieved_tflops / peaks["bf16_tflops"],
                 "traffic": (lambda b: None if b is None else b * T)(
-                    profiled_traffic("ncu_prefill_chunked_16x4096")),
+                    profiled_traffic("ncu_prefill_" + kernel_name + "_16x4096")),
                 "peak_source": peaks["source"],
-                "kernel": "gdn prefill (" + args.method + ")",
+                "kernel": "gdn prefill (" + kernel_name + ")",
                 "flops_per_launch": flops, "algorithmic_bytes_per_launch": pbytes,
                 "hbm_gbs_achieved": pbytes / avg_launch_s / 1e9,
                 "hbm_frac": pbytes / avg_launch_s / 1e9 / peaks["hbm_gbs"]}
@@ -349,7 +352,7 @@ def main():
                 "dtype": "bf16", "data": "synthetic (seeded; shapes and distributions of "
                                          "the benchmark configurations)",
                 "config": base_config(world), "roofline": roofline, "cpu_baseline": cpu,
-                "e2e": e2e, "gpu_launches": args.steps, "clocks": clk.summary(),
+                "e2e": e2e, "gpu_launches": args.steps * launches_per_step, "clocks": clk.summary(),
                 "decode": decode, "launch_ms": launch_ms}
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -28,8 +28,9 @@ GDN_PREFILL_RECURRENT = 2
 GDN_PREFILL_TCGEN05 = 3
 
 # Every symbol include/gdn_b200.h declares.
-EXPORTED_SYMBOLS = ("gdn_prefill", "gdn_prefill_ex", "gdn_decode", "gdn_device_status",
-                    "gdn_last_error", "gdn_version")
+EXPORTED_SYMBOLS = ("gdn_prefill", "gdn_prefill_ex", "gdn_prefill_ws", "gdn_prefill_workspace_size",
+                    "gdn_prefill_resolve",
+                    "gdn_decode", "gdn_device_status", "gdn_last_error", "gdn_version")
 
 _lock = threading.Lock()
 _lib = None
@@ -68,6 +69,12 @@ def load() -> ctypes.CDLL:
         lib.gdn_prefill.restype = i32
         lib.gdn_prefill_ex.argtypes = prefill_args + [i32, vp]
         lib.gdn_prefill_ex.restype = i32
+        lib.gdn_prefill_ws.argtypes = prefill_args + [i32, vp, ctypes.c_size_t, vp]
+        lib.gdn_prefill_ws.restype = i32
+        lib.gdn_prefill_resolve.argtypes = [i64, i32]
+        lib.gdn_prefill_resolve.restype = i32
+        lib.gdn_prefill_workspace_size.argtypes = [i64, i64, i32]
+        lib.gdn_prefill_workspace_size.restype = ctypes.c_size_t
         lib.gdn_decode.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i64, i32, i32, i32, f32,
                                    i32, i32, vp, vp, vp]
         lib.gdn_decode.restype = i32

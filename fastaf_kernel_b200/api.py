@@ -11,7 +11,9 @@ unchanged:
   * ``output=`` / ``new_state=`` preallocated destinations (the harness's
     destination-passing style, scripts/replay_first_workload.py:113-116);
   * ``kernel_decode(..., new_state=state)`` updates the state in place;
-  * ``method=`` chooses the prefill kernel (chunked tensor-core or recurrent).
+  * ``method=`` chooses the prefill kernel: "tcgen05" (chunk prep + chain kernels on
+    the 5th-generation tensor cores), "chunked" (mma.sync), "recurrent" (CUDA cores)
+    or "auto" (what ``prefill_method`` reports).
 """
 
 from __future__ import annotations
@@ -23,11 +25,21 @@ import torch
 
 from . import _lib
 
-__all__ = ["kernel", "kernel_decode", "kernel_dps", "kernel_decode_dps", "device_status"]
+__all__ = ["kernel", "kernel_decode", "kernel_dps", "kernel_decode_dps", "device_status",
+           "prefill_method"]
 
 _GATE_DTYPES = {torch.float32: _lib.GDN_DTYPE_F32, torch.bfloat16: _lib.GDN_DTYPE_BF16}
 _METHODS = {"auto": _lib.GDN_PREFILL_AUTO, "chunked": _lib.GDN_PREFILL_CHUNKED,
             "recurrent": _lib.GDN_PREFILL_RECURRENT, "tcgen05": _lib.GDN_PREFILL_TCGEN05}
+
+
+def prefill_method(total_tokens: int, method: str = "auto") -> str:
+    """Name of the prefill kernel a call with ``method`` runs for ``total_tokens``
+    packed tokens on the current CUDA device (the C library's own choice)."""
+    if method not in _METHODS:
+        raise ValueError(f"method must be one of {sorted(_METHODS)}")
+    code = _lib.load().gdn_prefill_resolve(int(total_tokens), _METHODS[method])
+    return {v: k for k, v in _METHODS.items()}[code]
 
 
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:

@@ -8,6 +8,7 @@
 #include <cstdio>
 #include <cmath>
 #include <cstring>
+#include <mutex>
 
 #include "gdn_b200.h"
 #include "gdn_common.cuh"
@@ -16,6 +17,7 @@
 namespace {
 
 thread_local char g_last_error[512] = "";
+constexpr int64_t kAutoTcMinTokens = 2048;
 
 int fail(int code, const char *fmt, ...) {
     va_list ap;
@@ -53,6 +55,39 @@ int check_common(int Hq, int Hv, int D, int gate_dtype, int param_dtype, const v
 int cuda_status(cudaError_t e, const char *what) {
     if (e == cudaSuccess) return GDN_OK;
     return fail(GDN_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// Stream-ordered workspace for callers that pass none: a library-owned memory pool
+// per device whose release threshold keeps its memory between calls, so a
+// steady-state call takes its workspace from the pool without a driver allocation.
+cudaError_t pool_alloc(void **ptr, size_t bytes, cudaStream_t stream) {
+    constexpr int kMaxDevices = 64;
+    static std::mutex mu;
+    static cudaMemPool_t pools[kMaxDevices] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    cudaMemPool_t pool;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (pools[dev] == nullptr) {
+            cudaMemPoolProps props;
+            std::memset(&props, 0, sizeof(props));
+            props.allocType = cudaMemAllocationTypePinned;
+            props.location.type = cudaMemLocationTypeDevice;
+            props.location.id = dev;
+            e = cudaMemPoolCreate(&pools[dev], &props);
+            if (e != cudaSuccess) {
+                pools[dev] = nullptr;
+                return e;
+            }
+            uint64_t keep = ~uint64_t(0);
+            cudaMemPoolSetAttribute(pools[dev], cudaMemPoolAttrReleaseThreshold, &keep);
+        }
+        pool = pools[dev];
+    }
+    return cudaMallocFromPoolAsync(ptr, bytes, pool, stream);
 }
 
 }  // namespace
@@ -97,12 +132,12 @@ int gdn_decode(const void *q, const void *k, const void *v, const float *state,
     return cuda_status(gdn::launch_decode(p, static_cast<cudaStream_t>(stream)), "gdn_decode launch");
 }
 
-int gdn_prefill_ex(const void *q, const void *k, const void *v, const float *state,
-                   const void *A_log, const void *a, const void *dt_bias, const void *b,
-                   const int32_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
-                   int num_qk_heads, int num_v_heads, int head_size, float scale,
-                   int gate_dtype, int param_dtype, void *output, float *new_state,
-                   int method, void *stream) {
+static int prefill_impl(const void *q, const void *k, const void *v, const float *state,
+                        const void *A_log, const void *a, const void *dt_bias, const void *b,
+                        const int32_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
+                        int num_qk_heads, int num_v_heads, int head_size, float scale,
+                        int gate_dtype, int param_dtype, void *output, float *new_state,
+                        int method, void *workspace, size_t workspace_bytes, void *stream) {
     g_last_error[0] = '\0';
     int rc = check_common(num_qk_heads, num_v_heads, head_size, gate_dtype, param_dtype, q, k, v,
                           A_log, a, dt_bias, b, output, new_state);
@@ -121,17 +156,36 @@ int gdn_prefill_ex(const void *q, const void *k, const void *v, const float *sta
     if (method != GDN_PREFILL_AUTO && method != GDN_PREFILL_CHUNKED && method != GDN_PREFILL_RECURRENT &&
         method != GDN_PREFILL_TCGEN05)
         return fail(GDN_ERR_INVALID_ARGUMENT, "unknown prefill method %d", method);
+    if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+        return fail(GDN_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
     if (num_seqs == 0) return GDN_OK;
     gdn::PrefillArgs p{q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs, total_tokens,
                        num_qk_heads, num_v_heads,
                        scale == 0.0f ? 1.0f / sqrtf(static_cast<float>(head_size)) : scale,
                        gate_dtype, param_dtype, output, new_state};
     const auto s = static_cast<cudaStream_t>(stream);
+    // auto: the tcgen05 pipeline for large batches; below ~2K tokens its extra prep
+    // launch does not pay off and the single-launch mma.sync kernel is faster.
+    if (method == GDN_PREFILL_AUTO && gdn_prefill_resolve(total_tokens, method) == GDN_PREFILL_TCGEN05)
+        method = GDN_PREFILL_TCGEN05;
     if (method == GDN_PREFILL_TCGEN05) {
         if (!gdn::prefill_tc_supported(p))
             return fail(GDN_ERR_UNSUPPORTED,
                         "the tcgen05 prefill needs an sm_100 device and total_tokens >= 64");
-        return cuda_status(gdn::launch_prefill_tc(p, s), "gdn_prefill (tcgen05) launch");
+        const size_t need = gdn::prefill_tc_workspace_bytes(p);
+        if (workspace) {
+            if (workspace_bytes < need)
+                return fail(GDN_ERR_INVALID_ARGUMENT, "workspace of %zu bytes is smaller than the %zu needed",
+                            workspace_bytes, need);
+            return cuda_status(gdn::launch_prefill_tc(p, workspace, s), "gdn_prefill (tcgen05) launch");
+        }
+        void *ws = nullptr;
+        cudaError_t e = pool_alloc(&ws, need, s);
+        if (e != cudaSuccess) return cuda_status(e, "gdn_prefill (tcgen05) workspace");
+        e = gdn::launch_prefill_tc(p, ws, s);
+        const cudaError_t ef = cudaFreeAsync(ws, s);
+        if (e != cudaSuccess) return cuda_status(e, "gdn_prefill (tcgen05) launch");
+        return cuda_status(ef, "gdn_prefill (tcgen05) workspace release");
     }
     const bool chunked_ok = gdn::prefill_chunked_supported(p);
     if (method == GDN_PREFILL_CHUNKED && !chunked_ok)
@@ -139,6 +193,47 @@ int gdn_prefill_ex(const void *q, const void *k, const void *v, const float *sta
     if (method == GDN_PREFILL_RECURRENT || (method == GDN_PREFILL_AUTO && !chunked_ok))
         return cuda_status(gdn::launch_prefill_recurrent(p, s), "gdn_prefill (recurrent) launch");
     return cuda_status(gdn::launch_prefill_chunked(p, s), "gdn_prefill (chunked) launch");
+}
+
+int gdn_prefill_ex(const void *q, const void *k, const void *v, const float *state,
+                   const void *A_log, const void *a, const void *dt_bias, const void *b,
+                   const int32_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
+                   int num_qk_heads, int num_v_heads, int head_size, float scale,
+                   int gate_dtype, int param_dtype, void *output, float *new_state,
+                   int method, void *stream) {
+    return prefill_impl(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs, total_tokens,
+                        num_qk_heads, num_v_heads, head_size, scale, gate_dtype, param_dtype, output,
+                        new_state, method, nullptr, 0, stream);
+}
+
+int gdn_prefill_ws(const void *q, const void *k, const void *v, const float *state,
+                   const void *A_log, const void *a, const void *dt_bias, const void *b,
+                   const int32_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
+                   int num_qk_heads, int num_v_heads, int head_size, float scale,
+                   int gate_dtype, int param_dtype, void *output, float *new_state,
+                   int method, void *workspace, size_t workspace_bytes, void *stream) {
+    return prefill_impl(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs, total_tokens,
+                        num_qk_heads, num_v_heads, head_size, scale, gate_dtype, param_dtype, output,
+                        new_state, method, workspace, workspace_bytes, stream);
+}
+
+int gdn_prefill_resolve(int64_t total_tokens, int method) {
+    gdn::PrefillArgs p{};
+    p.total_tokens = total_tokens;
+    if (method == GDN_PREFILL_AUTO) {
+        if (total_tokens >= kAutoTcMinTokens && gdn::prefill_tc_supported(p)) return GDN_PREFILL_TCGEN05;
+        return gdn::prefill_chunked_supported(p) ? GDN_PREFILL_CHUNKED : GDN_PREFILL_RECURRENT;
+    }
+    return method;
+}
+
+size_t gdn_prefill_workspace_size(int64_t num_seqs, int64_t total_tokens, int num_v_heads) {
+    if (num_seqs < 0 || total_tokens < 0 || num_v_heads <= 0) return 0;
+    gdn::PrefillArgs p{};
+    p.num_seqs = num_seqs;
+    p.total_tokens = total_tokens;
+    p.Hv = num_v_heads;
+    return gdn::prefill_tc_workspace_bytes(p);
 }
 
 int gdn_prefill(const void *q, const void *k, const void *v, const float *state,

@@ -23,26 +23,33 @@ __device__ __forceinline__ uint32_t swz(uint32_t row, uint32_t col) {
     return row * kRowBytes + ((((col >> 3) ^ (row & 7u))) << 4) + (col & 7u) * 2u;
 }
 
-// (I + A)^-1 for a 64x64 strictly-lower A (fp32, row-major, stride 64): the
+// (I + A)^-1 for a 64x64 strictly-lower A (fp32, row-major, row stride LD): the
 // 16x16 diagonal blocks by forward substitution, then the off-diagonal blocks
 // block-diagonal by block-diagonal as T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj.
-// Only the lower triangle (j <= i) of Tm is written.  All `nthreads` threads
-// of the block must call it; it synchronizes the block internally.
-template <int nthreads>
-__device__ void solve_unit_lower(const float *A, float *Tm, float *scr) {
+// Only the lower triangle (j <= i) of Tm (same stride) is written.  An odd LD
+// (65) keeps row-per-thread accesses free of bank conflicts.  All `nthreads`
+// threads of the block must call it; it synchronizes the block internally.
+template <int nthreads, int LD>
+__device__ __forceinline__ void solve_unit_lower(const float *A, float *Tm, float *scr) {
     const int tid = threadIdx.x;
     if (tid < 64) {
+        // Thread (block o, column c) solves column c of the diagonal block's inverse;
+        // two partial sums halve the dependent FMA chain of each row.
         const int o = (tid >> 4) * 16, c = tid & 15;
+        const float *Ab = A + o * LD + o;
         float x[16];
 #pragma unroll
         for (int r = 0; r < 16; ++r) {
-            float acc = (r == c) ? 1.0f : 0.0f;
+            float a0 = (r == c) ? 1.0f : 0.0f, a1 = 0.0f;
 #pragma unroll
-            for (int j = 0; j < r; ++j) acc = fmaf(-A[(o + r) * 64 + o + j], x[j], acc);
-            x[r] = acc;
+            for (int j = 0; j < r; ++j) {
+                if (j & 1) a1 = fmaf(-Ab[r * LD + j], x[j], a1);
+                else a0 = fmaf(-Ab[r * LD + j], x[j], a0);
+            }
+            x[r] = a0 + a1;
         }
 #pragma unroll
-        for (int r = 0; r < 16; ++r) Tm[(o + r) * 64 + o + c] = x[r];
+        for (int r = 0; r < 16; ++r) Tm[(o + r) * LD + o + c] = x[r];
     }
     __syncthreads();
     for (int d = 1; d < 4; ++d) {
@@ -51,22 +58,22 @@ __device__ void solve_unit_lower(const float *A, float *Tm, float *scr) {
             const int bi = d + (e >> 8), bj = bi - d, r = (e & 255) >> 4, cc = e & 15;
             float acc = 0.0f;
             for (int bk = bj; bk < bi; ++bk) {
-                const float *ar = A + (16 * bi + r) * 64 + 16 * bk;
-                const float *tc = Tm + (16 * bk) * 64 + 16 * bj + cc;
+                const float *ar = A + (16 * bi + r) * LD + 16 * bk;
+                const float *tc = Tm + (16 * bk) * LD + 16 * bj + cc;
 #pragma unroll
-                for (int kk = 0; kk < 16; ++kk) acc = fmaf(ar[kk], tc[kk * 64], acc);
+                for (int kk = 0; kk < 16; ++kk) acc = fmaf(ar[kk], tc[kk * LD], acc);
             }
             scr[e] = acc;
         }
         __syncthreads();
         for (int e = tid; e < nblk * 256; e += nthreads) {
             const int bi = d + (e >> 8), bj = bi - d, r = (e & 255) >> 4, cc = e & 15;
-            const float *tr = Tm + (16 * bi + r) * 64 + 16 * bi;
+            const float *tr = Tm + (16 * bi + r) * LD + 16 * bi;
             const float *m = scr + (e & ~255) + cc;
             float acc = 0.0f;
 #pragma unroll
             for (int kk = 0; kk < 16; ++kk) acc = fmaf(tr[kk], m[kk * 16], acc);
-            Tm[(16 * bi + r) * 64 + 16 * bj + cc] = -acc;
+            Tm[(16 * bi + r) * LD + 16 * bj + cc] = -acc;
         }
         __syncthreads();
     }

@@ -36,8 +36,12 @@ cudaError_t launch_decode(const DecodeArgs &p, cudaStream_t stream);
 cudaError_t launch_prefill_recurrent(const PrefillArgs &p, cudaStream_t stream);
 cudaError_t launch_prefill_chunked(const PrefillArgs &p, cudaStream_t stream);
 bool prefill_chunked_supported(const PrefillArgs &p);
-cudaError_t launch_prefill_tc(const PrefillArgs &p, cudaStream_t stream);
+// tcgen05 prefill: per-chunk prep (gdn_chunk_prep.cu) into `workspace` of
+// prefill_tc_workspace_bytes() bytes (256-byte aligned), then the chain kernel.
+cudaError_t launch_prefill_tc(const PrefillArgs &p, void *workspace, cudaStream_t stream);
 bool prefill_tc_supported(const PrefillArgs &p);
+size_t prefill_tc_workspace_bytes(const PrefillArgs &p);
+cudaError_t launch_chunk_prep(const PrefillArgs &p, float *ws_T, float *ws_g, cudaStream_t stream);
 // Site of the first bounded device wait of the tcgen05 prefill that gave up (0 = none).
 cudaError_t read_tc_device_error(cudaStream_t stream, int *code, bool clear);
 

@@ -16,13 +16,16 @@
 // their rows of T the identity and their innovations zero.  Every product with an
 // fp32 operand (S0, T, W, the decayed delta) splits it into bf16 hi + lo.
 //
+// The state-independent part of every chunk -- its gates and T -- is computed for
+// all chunks at once by gdn_chunk_prep.cu into a workspace (gdn_tc_workspace.h);
+// this kernel streams T and the gate vectors in with the chunk's q/k/v tiles.
+//
 // One CTA per (sequence, v-head) chain.  Warp roles:
 //   warp 0      allocates all 512 TMEM columns; lane 0 issues every TMA copy and MMA
-//   warps 0-3   shared-memory work: diag(Gamma) Q, the 64x64 inverse, T', T''
-//   warp 1      the gates of the chunk
+//   warps 0-3   shared-memory work: diag(Gamma) Q, T', T''
 //   warps 4-7   own TMEM lanes 0-127 (state row v / token row): every TMEM load/store
-// The fp32 state lives in TMEM columns [0,128) for the whole sequence; q/k/v tiles
-// are double-buffered so the copy of chunk c+1 overlaps chunk c.
+// The fp32 state lives in TMEM columns [0,128) for the whole sequence; the
+// per-chunk inputs are double-buffered so the copy of chunk c+1 overlaps chunk c.
 //
 // Every mbarrier wait is bounded (about 2 s).  A wait that gives up records its
 // site in g_tc_error; the CTA then stops at the next block barrier, waits
@@ -35,6 +38,7 @@
 #include "gdn_common.cuh"
 #include "gdn_launch.h"
 #include "sm100.cuh"
+#include "gdn_tc_workspace.h"
 #include "tma_host.h"
 
 namespace gdn {
@@ -61,11 +65,11 @@ constexpr uint32_t OFF_T2H = 136 * 1024;
 constexpr uint32_t OFF_T2L = 144 * 1024;
 constexpr uint32_t OFF_WH = 152 * 1024;     // 16 KB each: -W hi/lo, MN-major [k][i]
 constexpr uint32_t OFF_WL = 168 * 1024;
-constexpr uint32_t OFF_AF = OFF_WH;         // fp32 A [64][64] (aliases -W hi; never live together)
-constexpr uint32_t OFF_TF = OFF_WL;         // fp32 T [64][64] (aliases -W lo)
-constexpr uint32_t OFF_SCR = 184 * 1024;    // 3 KB: blocked-solve scratch
-constexpr uint32_t OFF_GATE = 188 * 1024;   // beta, gamma, Gamma: 3 x 64 fp32
-constexpr uint32_t SMEM_BYTES = 189 * 1024;
+constexpr uint32_t OFF_TST = 184 * 1024;    // 2 stages x 16 KB: fp32 T [64][64] from the workspace
+constexpr uint32_t OFF_GST = 216 * 1024;    // 2 stages x 1 KB: beta, gamma*log2(e), Gamma, exp(gamma_63 - gamma)
+constexpr uint32_t OFF_O = OFF_QS;          // bf16 [64][128] output staging (over diag(Gamma) Q)
+constexpr uint32_t SMEM_BYTES = 218 * 1024;
+constexpr uint32_t kStageTx = 6 * 8192 + kTcTileBytes + kTcGateBytes;   // bytes per chunk copy
 constexpr uint32_t SMEM_ALLOC = SMEM_BYTES + 1024;
 
 // TMEM columns (all 512 allocated).
@@ -92,13 +96,18 @@ struct TcParams {
     int gate_dtype, param_dtype;
     __nv_bfloat16 *out;
     float *new_state;
+    const float *ws_T, *ws_g;
 };
 
-// The six TMA copies of one chunk: k and q halves into [K_h0|Q_h0|K_h1|Q_h1], v halves.
+// The copies of one chunk: k and q halves into [K_h0|Q_h0|K_h1|Q_h1], v halves (TMA),
+// and the chunk's T and gate vectors from the workspace (bulk copies).
 __device__ __forceinline__ void issue_chunk(const CUtensorMap *qmap, const CUtensorMap *kmap,
                                             const CUtensorMap *vmap, uint32_t kq, uint32_t vv,
+                                            uint32_t ts, uint32_t gs, const float *wT, const float *wg,
                                             uint32_t bar, int z, int hq, int h) {
-    mbar_arrive_expect_tx(bar, 6 * 8192);
+    mbar_arrive_expect_tx(bar, kStageTx);
+    bulk_load(ts, wT, kTcTileBytes, bar);
+    bulk_load(gs, wg, kTcGateBytes, bar);
     tma_load_3d(kq, kmap, bar, 0, hq, z);
     tma_load_3d(kq + 8192, qmap, bar, 0, hq, z);
     tma_load_3d(kq + 16384, kmap, bar, 64, hq, z);
@@ -153,11 +162,6 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
     s1 = s1 < s0 ? s0 : (s1 > p.T ? p.T : s1);
     const int nch = static_cast<int>((s1 - s0 + kC - 1) / kC);
 
-    float *g_beta = reinterpret_cast<float *>(sm + OFF_GATE);
-    float *g_gam = g_beta + 64, *g_Gam = g_beta + 128;
-    float *A_f = reinterpret_cast<float *>(sm + OFF_AF);
-    float *T_f = reinterpret_cast<float *>(sm + OFF_TF);
-    float *scr = reinterpret_cast<float *>(sm + OFF_SCR);
     const uint32_t sbase = smem_u32(sm);
     const uint32_t b_tma0 = smem_u32(&bar_tma[0]), b_tma1 = smem_u32(&bar_tma[1]);
     const uint32_t b_mma = smem_u32(&bar_mma);
@@ -205,14 +209,14 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         }
         if (tid == 0) {
             for (int c = 0; c < 2 && c < nch; ++c) {
+                const int64_t unit = tc_slot(s0, c, n) * p.Hv + h;
                 issue_chunk(&qmap, &kmap, &vmap, sbase + OFF_KQ + c * KQ_STAGE, sbase + OFF_V + c * V_STAGE,
+                            sbase + OFF_TST + c * kTcTileBytes, sbase + OFF_GST + c * kTcGateBytes,
+                            p.ws_T + unit * (kTcTileBytes / 4), p.ws_g + unit * (kTcGateBytes / 4),
                             c ? b_tma1 : b_tma0, static_cast<int>(s0 + c * kC), hq, h);
                 ++tma_issued;
             }
         }
-        const float exp_A = expf(load_scalar(p.A_log, h, p.param_dtype));
-        const float dtb = load_scalar(p.dt_bias, h, p.param_dtype);
-
         for (int c = 0; c < nch; ++c) {
             const int st = c & 1;
             const int64_t t0 = s0 + static_cast<int64_t>(c) * kC;
@@ -220,33 +224,13 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             const uint32_t kq = sbase + OFF_KQ + st * KQ_STAGE;
             const uint32_t vv = sbase + OFF_V + st * V_STAGE;
 
-            // (1) gates (warp 1): beta, inclusive cumsum gamma of log alpha, Gamma
-            if (warp == 1) {
-                float lg[2], bt[2];
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const int i = lane + 32 * u;
-                    lg[u] = 0.0f;
-                    bt[u] = 0.0f;
-                    if (i < nt) {
-                        const int64_t gi = (t0 + i) * p.Hv + h;
-                        lg[u] = log_decay(exp_A, load_scalar(p.a, gi, p.gate_dtype), dtb);
-                        bt[u] = sigmoid_f(load_scalar(p.b, gi, p.gate_dtype));
-                    }
-                }
-                float x0 = lg[0], x1 = lg[1];
-#pragma unroll
-                for (int off = 1; off < 32; off <<= 1) {
-                    const float y0 = __shfl_up_sync(0xffffffffu, x0, off);
-                    const float y1 = __shfl_up_sync(0xffffffffu, x1, off);
-                    if (lane >= off) { x0 += y0; x1 += y1; }
-                }
-                x1 += __shfl_sync(0xffffffffu, x0, 31);
-                g_beta[lane] = bt[0]; g_beta[lane + 32] = bt[1];
-                g_gam[lane] = x0; g_gam[lane + 32] = x1;
-                g_Gam[lane] = expf(x0); g_Gam[lane + 32] = expf(x1);
-            }
-            __syncthreads();
+            // (1) this chunk's tiles, T and gates (every thread reads the gate vectors)
+            ok = wait_phase(st ? b_tma1 : b_tma0, (c >> 1) & 1, kWaitTma);
+            if (tid == 0 && ok) ++tma_done;
+            if (!block_sync_ok(ok)) break;
+            const float *g_beta = reinterpret_cast<const float *>(sm + OFF_GST + st * kTcGateBytes);
+            const float *g_gam2 = g_beta + 64, *g_Gam = g_beta + 128, *g_dec = g_beta + 192;
+            const float *T_s = reinterpret_cast<const float *>(sm + OFF_TST + st * kTcTileBytes);
 
             if (owner) {
                 // (2) S -> bf16 hi/lo (TMEM A operands); S <- Gamma_63 * S
@@ -271,10 +255,8 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                     tmem_wait_st();
                 }
             } else {
-                // (3) this chunk's tiles; [K;Q] K^T on the tensor core; diag(Gamma) Q
-                ok = wait_phase(st ? b_tma1 : b_tma0, (c >> 1) & 1, kWaitTma);
-                if (tid == 0 && ok) {
-                    ++tma_done;
+                // (3) [K;Q] K^T on the tensor core (its Q K^T rows); diag(Gamma) Q
+                if (tid == 0) {
                     const uint32_t id = idesc_bf16_f32(128, 64, false, false);
 #pragma unroll
                     for (int s = 0; s < 8; ++s) {
@@ -303,46 +285,35 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             }
             if (!block_sync_ok(ok)) break;
 
-            // (4) A = strict_lower(beta_i exp(gamma_i - gamma_j) K K^T) (owner lanes 0-63),
-            //     P = lower(exp(gamma_i - gamma_j) Q K^T) (owner lanes 64-127)
+            // (4) P = lower(exp(gamma_i - gamma_j) Q K^T) (owner lanes 64-127)
             ok = wait_phase(b_mma, mma_phase, kWaitKK);
             if (ok) { mma_phase ^= 1; mma_inflight = false; }
-            if (owner) {
-                const int i = v & 63;
-                const float gi = g_gam[i], bi = g_beta[i];
+            if (owner && v >= 64) {
+                const int i = v - 64;
+                const float gi = g_gam2[i];
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {
                     uint32_t r[32];
                     tmem_ld32(tmem_addr(tm, lane_base, TM_KK + 32 * hf), r);
                     tmem_wait_ld_dep(r);
-                    if (v < 64) {
 #pragma unroll
-                        for (int jj = 0; jj < 32; ++jj) {
-                            const int j = 32 * hf + jj;
-                            A_f[i * 64 + j] = j < i ? bi * expf(gi - g_gam[j]) * __uint_as_float(r[jj]) : 0.0f;
+                    for (int cq = 0; cq < 4; ++cq) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int jj = cq * 8 + 2 * e, j0 = 32 * hf + jj, j1 = j0 + 1;
+                            const float p0 = j0 <= i ? exp2f(gi - g_gam2[j0]) * __uint_as_float(r[jj]) : 0.0f;
+                            const float p1 = j1 <= i ? exp2f(gi - g_gam2[j1]) * __uint_as_float(r[jj + 1]) : 0.0f;
+                            w[e] = pack_bf16x2(p0, p1);
                         }
-                    } else {
-#pragma unroll
-                        for (int cq = 0; cq < 4; ++cq) {
-                            uint32_t w[4];
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                const int jj = cq * 8 + 2 * e, j0 = 32 * hf + jj, j1 = j0 + 1;
-                                const float p0 = j0 <= i ? expf(gi - g_gam[j0]) * __uint_as_float(r[jj]) : 0.0f;
-                                const float p1 = j1 <= i ? expf(gi - g_gam[j1]) * __uint_as_float(r[jj + 1]) : 0.0f;
-                                w[e] = pack_bf16x2(p0, p1);
-                            }
-                            *reinterpret_cast<uint4 *>(sm + OFF_P + sw128(i, 4 * hf + cq)) =
-                                make_uint4(w[0], w[1], w[2], w[3]);
-                        }
+                        *reinterpret_cast<uint4 *>(sm + OFF_P + sw128(i, 4 * hf + cq)) =
+                            make_uint4(w[0], w[1], w[2], w[3]);
                     }
                 }
                 fence_proxy_async_smem();
             }
-            if (!block_sync_ok(ok)) break;
 
-            // (5) T = (I + A)^-1; T' = T diag(beta), T'' = T diag(beta Gamma) as bf16 hi/lo
-            solve_unit_lower<kThreads>(A_f, T_f, scr);
+            // (5) T' = T diag(beta), T'' = T diag(beta Gamma) as bf16 hi/lo (T from the workspace)
             {
                 const int i = tid >> 2, qd = tid & 3;
 #pragma unroll
@@ -355,7 +326,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
 #pragma unroll
                         for (int u = 0; u < 2; ++u) {
                             const int j = ch * 8 + 2 * e + u;
-                            const float t = j <= i ? T_f[i * 64 + j] : 0.0f;
+                            const float t = T_s[i * 64 + j];
                             v1[u] = t * g_beta[j];
                             v2[u] = v1[u] * g_Gam[j];
                         }
@@ -373,7 +344,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                 }
             }
             fence_proxy_async_smem();
-            block_sync_tc();
+            if (!block_sync_ok(ok)) break;
 
             // (6) W^T = K^T T''^T (lanes k), U^T = V^T T'^T (lanes v)
             if (tid == 0) {
@@ -449,7 +420,6 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
 
             // (9) delta -> bf16 (output path), exp(gamma_63 - gamma_i) delta -> hi/lo (state path)
             if (owner) {
-                const float gamC = g_gam[63];
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
                     uint32_t r[32], db[16], dh[16], dl[16];
@@ -461,8 +431,8 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                         const float d0 = __uint_as_float(r[2 * e]), d1 = __uint_as_float(r[2 * e + 1]);
                         db[e] = pack_bf16x2(d0, d1);
                         float h0, l0, h1, l1;
-                        split_bf16(d0 * expf(gamC - g_gam[i0]), h0, l0);
-                        split_bf16(d1 * expf(gamC - g_gam[i1]), h1, l1);
+                        split_bf16(d0 * g_dec[i0], h0, l0);
+                        split_bf16(d1 * g_dec[i1], h1, l1);
                         dh[e] = pack_bf16x2(h0, h1);
                         dl[e] = pack_bf16x2(l0, l1);
                     }
@@ -494,28 +464,34 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             ok = wait_phase(b_mma, mma_phase, kWaitUpd);
             if (ok) { mma_phase ^= 1; mma_inflight = false; }
 
-            // (11) this chunk's output rows; refill this stage with chunk c+2
+            // (11) this chunk's output: owner lane v -> column v of a bf16 [i][v] tile,
+            //      then coalesced 16-byte row stores; refill this stage with chunk c+2
             if (owner) {
-                __nv_bfloat16 *o = p.out + (t0 * p.Hv + h) * kHeadDim + v;
-                const int64_t stride = static_cast<int64_t>(p.Hv) * kHeadDim;
+                __nv_bfloat16 *so = reinterpret_cast<__nv_bfloat16 *>(sm + OFF_O) + v;
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {
                     uint32_t r[32];
                     tmem_ld32(tmem_addr(tm, lane_base, TM_D1B + 32 * hf), r);
                     tmem_wait_ld_dep(r);
 #pragma unroll
-                    for (int ii = 0; ii < 32; ++ii) {
-                        const int i = 32 * hf + ii;
-                        if (i < nt) o[i * stride] = __float2bfloat16_rn(p.scale * __uint_as_float(r[ii]));
-                    }
+                    for (int ii = 0; ii < 32; ++ii)
+                        so[(32 * hf + ii) * kHeadDim] = __float2bfloat16_rn(p.scale * __uint_as_float(r[ii]));
                 }
             }
             if (tid == 0 && ok && c + 2 < nch) {
-                issue_chunk(&qmap, &kmap, &vmap, kq, vv, st ? b_tma1 : b_tma0,
+                const int64_t unit = tc_slot(s0, c + 2, n) * p.Hv + h;
+                issue_chunk(&qmap, &kmap, &vmap, kq, vv, sbase + OFF_TST + st * kTcTileBytes,
+                            sbase + OFF_GST + st * kTcGateBytes, p.ws_T + unit * (kTcTileBytes / 4),
+                            p.ws_g + unit * (kTcGateBytes / 4), st ? b_tma1 : b_tma0,
                             static_cast<int>(t0 + 2 * kC), hq, h);
                 ++tma_issued;
             }
             if (!block_sync_ok(ok)) break;
+            for (int idx = tid; idx < nt * 16; idx += kThreads) {
+                const int i = idx >> 4, c16 = idx & 15;
+                const uint4 val = *reinterpret_cast<const uint4 *>(sm + OFF_O + i * 256 + c16 * 16);
+                *reinterpret_cast<uint4 *>(p.out + ((t0 + i) * p.Hv + h) * kHeadDim + c16 * 8) = val;
+            }
         }
 
         if (ok && owner) {   // final state: TMEM -> new_state (owner lane v writes row v)
@@ -565,10 +541,18 @@ bool prefill_tc_supported(const PrefillArgs &p) {
     return p.total_tokens >= kC && p.total_tokens < (int64_t(1) << 31) && is_sm100();
 }
 
-cudaError_t launch_prefill_tc(const PrefillArgs &p, cudaStream_t stream) {
+size_t prefill_tc_workspace_bytes(const PrefillArgs &p) {
+    return static_cast<size_t>(tc_workspace_bytes(p.total_tokens, p.num_seqs, p.Hv));
+}
+
+// Two launches on `stream`: the per-chunk prep of every chunk, then the chains.
+cudaError_t launch_prefill_tc(const PrefillArgs &p, void *workspace, cudaStream_t stream) {
     const int64_t ctas = p.num_seqs * p.Hv;
     if (ctas == 0) return cudaSuccess;
     if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+    float *ws_T = static_cast<float *>(workspace);
+    float *ws_g = reinterpret_cast<float *>(static_cast<char *>(workspace) +
+                                            tc_num_slots(p.total_tokens, p.num_seqs) * p.Hv * kTcTileBytes);
     CUtensorMap qm, km, vm;
     std::memset(&qm, 0, sizeof(qm));
     std::memset(&km, 0, sizeof(km));
@@ -577,12 +561,13 @@ cudaError_t launch_prefill_tc(const PrefillArgs &p, cudaStream_t stream) {
         !make_tmap_thd_bf16(&km, p.k, p.total_tokens, p.Hq) ||
         !make_tmap_thd_bf16(&vm, p.v, p.total_tokens, p.Hv))
         return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         SMEM_ALLOC);
+    cudaError_t e = launch_chunk_prep(p, ws_T, ws_g, stream);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC);
     if (e != cudaSuccess) return e;
     TcParams tp{p.state, p.A_log, p.a, p.dt_bias, p.b, p.cu_seqlens, p.total_tokens, p.Hq, p.Hv,
                 p.scale, p.gate_dtype, p.param_dtype, static_cast<__nv_bfloat16 *>(p.out),
-                p.new_state};
+                p.new_state, ws_T, ws_g};
     prefill_tc_kernel<<<static_cast<unsigned>(ctas), kThreads, SMEM_ALLOC, stream>>>(qm, km, vm, tp);
     return cudaGetLastError();
 }

@@ -1,0 +1,36 @@
+// gdn_tc_workspace.h -- layout of the per-chunk workspace the tcgen05 prefill
+// shares between its two kernels (gdn_chunk_prep.cu writes, gdn_prefill_tc.cu reads).
+//
+// Chunk c of sequence n (tokens [s0 + 64c, s0 + 64c + 64) with s0 = cu_seqlens[n])
+// owns the slot  floor(s0 / 64) + c + n.  Slots of consecutive chunks and of
+// consecutive sequences never collide (a sequence of L tokens starting at s0 ends
+// at or after slot floor(s0/64) + ceil(L/64) - 1 + n, and the next one starts at
+// floor((s0 + L)/64) + n + 1 or later), and every slot is below ceil(T/64) + N,
+// so the workspace is sized from T and N alone, without reading cu_seqlens.
+//
+// Per (slot, v-head):  T = (I + A)^-1 as fp32 [64][64] row-major, zero above the
+// diagonal (16 KB), then, in a second array, the chunk's gate vectors as four
+// fp32 [64] rows: beta, gamma * log2(e), Gamma = exp(gamma), exp(gamma_63 - gamma)
+// (1 KB).  Padding tokens of a partial chunk have beta = 0 and log alpha = 0.
+#pragma once
+
+#include <stdint.h>
+
+namespace gdn {
+
+constexpr int64_t kTcTileBytes = 64 * 64 * 4;
+constexpr int64_t kTcGateBytes = 4 * 64 * 4;
+
+__host__ __device__ inline int64_t tc_num_slots(int64_t total_tokens, int64_t num_seqs) {
+    return (total_tokens + 63) / 64 + num_seqs;
+}
+
+__host__ __device__ inline int64_t tc_workspace_bytes(int64_t total_tokens, int64_t num_seqs, int Hv) {
+    return tc_num_slots(total_tokens, num_seqs) * Hv * (kTcTileBytes + kTcGateBytes);
+}
+
+__host__ __device__ inline int64_t tc_slot(int64_t s0, int c, int64_t n) {
+    return s0 / 64 + c + n;
+}
+
+}  // namespace gdn

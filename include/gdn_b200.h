@@ -19,6 +19,7 @@
 #ifndef GDN_B200_H_
 #define GDN_B200_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #if defined(__GNUC__)
@@ -43,7 +44,7 @@ extern "C" {
 #define GDN_DTYPE_BF16 1
 
 /* Prefill kernel choice for gdn_prefill_ex(). */
-#define GDN_PREFILL_AUTO 0      /* chunked tensor-core kernel when supported */
+#define GDN_PREFILL_AUTO 0      /* TCGEN05 from 2048 packed tokens, else CHUNKED, else RECURRENT */
 #define GDN_PREFILL_CHUNKED 1   /* chunked (C=64) WY/UT kernel on the tensor cores (mma.sync) */
 #define GDN_PREFILL_RECURRENT 2 /* token-serial CUDA-core kernel */
 #define GDN_PREFILL_TCGEN05 3   /* chunked (C=64) kernel on tcgen05 + TMEM + TMA; T >= 64 */
@@ -88,6 +89,33 @@ GDN_API int gdn_prefill_ex(const void *q, const void *k, const void *v, const fl
                    int num_qk_heads, int num_v_heads, int head_size, float scale,
                    int gate_dtype, int param_dtype, void *output, float *new_state,
                    int method, void *stream);
+
+/*
+ * gdn_prefill_ex with a caller-provided workspace (no allocation inside the call).
+ *
+ * The GDN_PREFILL_TCGEN05 kernel computes each chunk's gates and T = (I + A)^-1 for
+ * all chunks at once into a workspace before it runs the chains; gdn_prefill and
+ * gdn_prefill_ex take that workspace from a library-owned stream-ordered memory pool,
+ * this entry point takes it from the caller.  `workspace` must be 256-byte aligned
+ * and hold gdn_prefill_workspace_size() bytes; other methods ignore it.  The
+ * workspace must not be reused by other work until the call's stream reaches it.
+ * No counterpart in the reference (its Triton kernel keeps no workspace).
+ */
+GDN_API int gdn_prefill_ws(const void *q, const void *k, const void *v, const float *state,
+                   const void *A_log, const void *a, const void *dt_bias, const void *b,
+                   const int32_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
+                   int num_qk_heads, int num_v_heads, int head_size, float scale,
+                   int gate_dtype, int param_dtype, void *output, float *new_state,
+                   int method, void *workspace, size_t workspace_bytes, void *stream);
+
+/* The prefill kernel (GDN_PREFILL_*) a call with `method` runs for `total_tokens` packed
+ * tokens on the current device: AUTO resolves to TCGEN05, CHUNKED or RECURRENT; other
+ * values are returned unchanged.  No counterpart in the reference. */
+GDN_API int gdn_prefill_resolve(int64_t total_tokens, int method);
+
+/* Workspace bytes gdn_prefill_ws needs for GDN_PREFILL_TCGEN05:
+ * (ceil(total_tokens / 64) + num_seqs) * num_v_heads * 17408.  No counterpart in the reference. */
+GDN_API size_t gdn_prefill_workspace_size(int64_t num_seqs, int64_t total_tokens, int num_v_heads);
 
 /*
  * Single-token decode.

@@ -178,3 +178,45 @@ def test_prefill_output_destination_passing():
     torch.cuda.synchronize()
     ro, rs = _oracle(x)
     assert_parity(out.cpu(), ro, ns.cpu(), rs)
+
+
+def test_auto_method_resolution():
+    """auto runs the tcgen05 pipeline from 2048 packed tokens, the mma.sync kernel below."""
+    assert fk.prefill_method(2048) == "tcgen05"
+    assert fk.prefill_method(131072) == "tcgen05"
+    assert fk.prefill_method(2047) == "chunked"
+    assert fk.prefill_method(1) == "chunked"
+    assert fk.prefill_method(5000, "recurrent") == "recurrent"
+
+
+def test_prefill_caller_workspace():
+    """gdn_prefill_ws with a caller-provided workspace equals the pooled-workspace call."""
+    import ctypes
+    from fastaf_kernel_b200 import _lib
+    x = W.prefill_inputs([300, 70, 129], seed=21, Hq=4, Hv=8)
+    g = _gpu(x)
+    o_ref, s_ref = fk.kernel(g["q"], g["k"], g["v"], g["state"], g["A_log"], g["a"], g["dt_bias"],
+                             g["b"], g["cu_seqlens"], g["scale"], method="tcgen05")
+    lib = _lib.load()
+    T, N = g["q"].shape[0], 3
+    nbytes = lib.gdn_prefill_workspace_size(N, T, 8)
+    assert nbytes == ((T + 63) // 64 + N) * 8 * 17408
+    ws = torch.full((nbytes // 4,), float("nan"), device=DEV)
+    out = torch.empty_like(o_ref)
+    ns = torch.empty_like(s_ref)
+    rc = lib.gdn_prefill_ws(g["q"].data_ptr(), g["k"].data_ptr(), g["v"].data_ptr(), g["state"].data_ptr(),
+                            g["A_log"].data_ptr(), g["a"].data_ptr(), g["dt_bias"].data_ptr(),
+                            g["b"].data_ptr(), g["cu_seqlens"].data_ptr(), N, T, 4, 8, 128,
+                            float(g["scale"]), _lib.GDN_DTYPE_BF16, _lib.GDN_DTYPE_F32, out.data_ptr(),
+                            ns.data_ptr(), _lib.GDN_PREFILL_TCGEN05, ws.data_ptr(), nbytes,
+                            torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, lib.gdn_last_error()
+    small = lib.gdn_prefill_ws(g["q"].data_ptr(), g["k"].data_ptr(), g["v"].data_ptr(), g["state"].data_ptr(),
+                               g["A_log"].data_ptr(), g["a"].data_ptr(), g["dt_bias"].data_ptr(),
+                               g["b"].data_ptr(), g["cu_seqlens"].data_ptr(), N, T, 4, 8, 128,
+                               float(g["scale"]), _lib.GDN_DTYPE_BF16, _lib.GDN_DTYPE_F32, out.data_ptr(),
+                               ns.data_ptr(), _lib.GDN_PREFILL_TCGEN05, ws.data_ptr(), nbytes - 16,
+                               torch.cuda.current_stream().cuda_stream)
+    assert small == _lib.GDN_ERR_INVALID_ARGUMENT
+    fk.device_status()
+    assert torch.equal(out, o_ref) and torch.equal(ns, s_ref)
