@@ -29,7 +29,7 @@ GDN_PREFILL_TCGEN05 = 3
 
 # Every symbol include/gdn_b200.h declares.
 EXPORTED_SYMBOLS = ("gdn_prefill", "gdn_prefill_ex", "gdn_prefill_ws", "gdn_prefill_workspace_size",
-                    "gdn_prefill_resolve",
+                    "gdn_prefill_resolve", "gdn_prefill_noalloc",
                     "gdn_decode", "gdn_device_status", "gdn_last_error", "gdn_version")
 
 _lock = threading.Lock()
@@ -71,6 +71,8 @@ def load() -> ctypes.CDLL:
         lib.gdn_prefill_ex.restype = i32
         lib.gdn_prefill_ws.argtypes = prefill_args + [i32, vp, ctypes.c_size_t, vp]
         lib.gdn_prefill_ws.restype = i32
+        lib.gdn_prefill_noalloc.argtypes = prefill_args + [vp]
+        lib.gdn_prefill_noalloc.restype = i32
         lib.gdn_prefill_resolve.argtypes = [i64, i32]
         lib.gdn_prefill_resolve.restype = i32
         lib.gdn_prefill_workspace_size.argtypes = [i64, i64, i32]

@@ -92,6 +92,10 @@ cudaError_t pool_alloc(void **ptr, size_t bytes, cudaStream_t stream) {
 
 }  // namespace
 
+namespace gdn {
+void set_last_error(const char *msg) { std::snprintf(g_last_error, sizeof(g_last_error), "%s", msg); }
+}  // namespace gdn
+
 extern "C" {
 
 const char *gdn_last_error(void) { return g_last_error; }

@@ -32,6 +32,9 @@ struct PrefillArgs {
     float *new_state;            // fp32 [N, Hv, D, D]
 };
 
+// Set the message gdn_last_error() returns on this thread.
+void set_last_error(const char *msg);
+
 cudaError_t launch_decode(const DecodeArgs &p, cudaStream_t stream);
 cudaError_t launch_prefill_recurrent(const PrefillArgs &p, cudaStream_t stream);
 cudaError_t launch_prefill_chunked(const PrefillArgs &p, cudaStream_t stream);

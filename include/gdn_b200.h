@@ -108,6 +108,29 @@ GDN_API int gdn_prefill_ws(const void *q, const void *k, const void *v, const fl
                    int gate_dtype, int param_dtype, void *output, float *new_state,
                    int method, void *workspace, size_t workspace_bytes, void *stream);
 
+/*
+ * gdn_prefill on the GDN_PREFILL_TCGEN05 kernel without any device allocation: its
+ * per-chunk workspace is a fixed 64 MiB device array inside this library.  For callers
+ * that must not allocate while serving (all device memory reserved by their own pools,
+ * no driver allocation allowed on a latency-critical path, or memory accounting that
+ * forbids allocations outside their allocator).  Same arguments and contract as
+ * gdn_prefill; additionally requires
+ *   (ceil(total_tokens / 64) + num_seqs) * num_v_heads * 17408 <= 64 MiB
+ * (e.g. 7168 tokens in up to 8 sequences with 32 v-heads) and total_tokens >= 64;
+ * larger calls return GDN_ERR_INVALID_ARGUMENT before any launch.  The first call on
+ * each device resolves the array's address (cudaGetSymbolAddress with that device
+ * current); make that first call before any stream capture that would include it.
+ * There is one array per device: calls whose executions overlap on the device (other
+ * streams, other host threads) race on it.
+ * No counterpart in the reference (its Triton kernel keeps no workspace).
+ */
+GDN_API int gdn_prefill_noalloc(const void *q, const void *k, const void *v, const float *state,
+                        const void *A_log, const void *a, const void *dt_bias, const void *b,
+                        const int32_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
+                        int num_qk_heads, int num_v_heads, int head_size, float scale,
+                        int gate_dtype, int param_dtype, void *output, float *new_state,
+                        void *stream);
+
 /* The prefill kernel (GDN_PREFILL_*) a call with `method` runs for `total_tokens` packed
  * tokens on the current device: AUTO resolves to TCGEN05, CHUNKED or RECURRENT; other
  * values are returned unchanged.  No counterpart in the reference. */
