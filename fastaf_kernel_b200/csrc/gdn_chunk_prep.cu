@@ -1,12 +1,13 @@
 // gdn_chunk_prep.cu -- the state-independent half of the chunked prefill, for every
 // chunk of every sequence at once: the chunk's gates and T = (I + A)^-1, written to
 // the workspace of gdn_tc_workspace.h that the tcgen05 chain kernel
-// (gdn_prefill_tc.cu) streams in.
+// (gdn_prefill_tc.cu) streams in, together with the chunk's decayed Q K^T tile P.
 //
 // For a chunk of tokens i, j = 0..63 (solution/gdn_baseline_torch.py:42-44, 71-87):
 //   log alpha_i = -exp(A_log) softplus(a_i + dt_bias),  beta_i = sigmoid(b_i)
 //   gamma_i = sum_{j<=i} log alpha_j,   Gamma_i = exp(gamma_i)
 //   A[i][j] = beta_i exp(gamma_i - gamma_j) k_i.k_j  (j < i),   T = (I + A)^-1
+//   P[i][j] = exp(gamma_i - gamma_j) q_i.k_j            (j <= i)
 // None of it depends on the recurrent state, so all chunks run in parallel here and
 // the chain kernel keeps only the state path on its serial critical path.
 //
@@ -40,8 +41,8 @@ constexpr uint32_t OFF_AH = 2 * 64 * 256;              // bf16 [64][64] A hi/lo 
 constexpr uint32_t OFF_AL = OFF_AH + 8192;
 constexpr uint32_t OFF_TH = OFF_AL + 8192;             // bf16 [64][64] T hi/lo
 constexpr uint32_t OFF_TL = OFF_TH + 8192;
-constexpr uint32_t OFF_SH = OFF_TL + 8192;             // bf16 [64][64] intermediate products hi/lo
-constexpr uint32_t OFF_SL = OFF_SH + 8192;
+constexpr uint32_t OFF_SH = OFF_TL + 8192;             // bf16 [64][64] intermediate products hi/lo;
+constexpr uint32_t OFF_SL = OFF_SH + 8192;             // before them, the Q tile [64][128] (16 KB)
 constexpr uint32_t OFF_AD = OFF_SL + 8192;             // fp32 diagonal blocks of A: 4 x [16][17]
 constexpr uint32_t OFF_T = OFF_AD + 4 * 16 * 17 * 4;   // fp32 T [64][65]
 constexpr uint32_t OFF_GATE = OFF_T + 64 * kLD * 4;    // beta, gamma*log2(e), Gamma, decay-to-end
@@ -89,6 +90,8 @@ __device__ __forceinline__ void store16(const float (&acc)[2][4], float sgn, uin
         }
 }
 
+// A [64][128] bf16 tile (rows t0.., head hq) into 256-byte swizzled rows; rows past T
+// read as zero.  One cp.async group.
 __device__ __forceinline__ void load_k_tile(uint32_t sK, const __nv_bfloat16 *k, int64_t T, int Hq, int hq,
                                             int64_t t0, int tid) {
 #pragma unroll
@@ -104,13 +107,14 @@ __device__ __forceinline__ void load_k_tile(uint32_t sK, const __nv_bfloat16 *k,
 }
 
 struct PrepParams {
-    const __nv_bfloat16 *k;
+    const __nv_bfloat16 *q, *k;
     const void *A_log, *a, *dt_bias, *b;
     const int32_t *cu_seqlens;
     int64_t T;
     int Hq, Hv, groups;
     int gate_dtype, param_dtype;
     float *ws_T, *ws_g;
+    __nv_bfloat16 *ws_P;
 };
 
 __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(const PrepParams p) {
@@ -142,12 +146,15 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(const PrepParam
         const int64_t t0 = s0 + static_cast<int64_t>(c) * kC;
         const int nt = static_cast<int>(s1 - t0 < kC ? s1 - t0 : kC);
         const uint32_t sK = sbase + OFF_K + (it & 1) * (64 * 256);
+        // This chunk's Q tile into the intermediate-product tiles (free until the products),
+        // then the next chunk's K tile into the other K buffer.
+        load_k_tile(sbase + OFF_SH, p.q, p.T, p.Hq, hq, t0, tid);
         const int cn = c + p.groups;
         if (cn < nch)
             load_k_tile(sbase + OFF_K + ((it + 1) & 1) * (64 * 256), p.k, p.T, p.Hq, hq,
                         s0 + static_cast<int64_t>(cn) * kC, tid);
 
-        // Gates (warp 0) while the tile is in flight.
+        // Gates (warp 0) while the tiles are in flight.
         if (warp == 0) {
             float lg[2], bt[2];
 #pragma unroll
@@ -176,7 +183,8 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(const PrepParam
             g_Gam[lane] = expf(x0); g_Gam[lane + 32] = expf(x1);
             g_dec[lane] = expf(xC - x0); g_dec[lane + 32] = expf(xC - x1);
         }
-        if (cn < nch) cp_async_wait<1>(); else cp_async_wait<0>();
+        // cp.async groups, oldest first: this chunk's K, its Q, [the next chunk's K].
+        if (cn < nch) cp_async_wait<2>(); else cp_async_wait<1>();
         __syncthreads();
 
         // K K^T: warp w computes rows 16*(w&3).. and columns 32*(w>>2).. on mma.sync;
@@ -261,6 +269,44 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(const PrepParam
         }
         __syncthreads();
 
+        // Q K^T on mma.sync, same warp tiling as K K^T; P (bf16, swizzled) straight to the workspace.
+        const int64_t unit = tc_slot(s0, c, n) * p.Hv + h;
+        if (cn < nch) cp_async_wait<1>(); else cp_async_wait<0>();
+        __syncthreads();
+        {
+            const uint32_t sQ = sbase + OFF_SH;
+            const int r0 = (warp & 3) * 16, c0 = (warp >> 2) * 32;
+            float acc[4][4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                uint32_t af[4];
+                ldsm_x4(af, a_addr<256>(sQ, r0, kk * 16, lane));
+#pragma unroll
+                for (int np = 0; np < 2; ++np) {
+                    uint32_t bf[4];
+                    ldsm_x4(bf, b_addr_nk<256>(sK, c0 + np * 16, kk * 16, lane));
+                    mma16816(acc[2 * np], af, bf[0], bf[1]);
+                    mma16816(acc[2 * np + 1], af, bf[2], bf[3]);
+                }
+            }
+            uint8_t *dP = reinterpret_cast<uint8_t *>(p.ws_P) + unit * kTcPBytes;
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                const int i = r0 + g + 8 * half;
+                const float gi = g_gam2[i];
+#pragma unroll
+                for (int ntl = 0; ntl < 4; ++ntl) {
+                    const int j = c0 + ntl * 8 + 2 * t4;
+                    const float p0 = j <= i ? exp2f(gi - g_gam2[j]) * acc[ntl][2 * half] : 0.0f;
+                    const float p1 = j + 1 <= i ? exp2f(gi - g_gam2[j + 1]) * acc[ntl][2 * half + 1] : 0.0f;
+                    *reinterpret_cast<uint32_t *>(dP + swz<128>(i, j)) = pack_bf16x2(p0, p1);
+                }
+            }
+        }
+        __syncthreads();   // the Q tile is dead; the products below reuse its space
+
         const uint32_t Ah = sbase + OFF_AH, Al = sbase + OFF_AL, Th = sbase + OFF_TH, Tl = sbase + OFF_TL;
         const uint32_t Sh = sbase + OFF_SH, Sl = sbase + OFF_SL;
         // M_10 = A_10 D_0 (warp 0), M_32 = A_32 D_2 (warp 1)
@@ -305,7 +351,6 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(const PrepParam
         __syncthreads();
 
         // T (row-major, zero above the diagonal) and the gate vectors to the workspace.
-        const int64_t unit = tc_slot(s0, c, n) * p.Hv + h;
         float *dT = p.ws_T + unit * (kTcTileBytes / 4);
 #pragma unroll
         for (int u = 0; u < (64 * 16) / kThreads; ++u) {
@@ -332,7 +377,8 @@ int prep_groups(int64_t chains) {
     return static_cast<int>(gsz < 1 ? 1 : (gsz > 64 ? 64 : gsz));
 }
 
-cudaError_t launch_chunk_prep(const PrefillArgs &p, float *ws_T, float *ws_g, cudaStream_t stream) {
+cudaError_t launch_chunk_prep(const PrefillArgs &p, float *ws_T, __nv_bfloat16 *ws_P, float *ws_g,
+                              cudaStream_t stream) {
     const int64_t chains = p.num_seqs * p.Hv;
     if (chains == 0) return cudaSuccess;
     if (chains > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
@@ -340,8 +386,9 @@ cudaError_t launch_chunk_prep(const PrefillArgs &p, float *ws_T, float *ws_g, cu
     cudaError_t e = cudaFuncSetAttribute(chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    PrepParams pp{static_cast<const __nv_bfloat16 *>(p.k), p.A_log, p.a, p.dt_bias, p.b, p.cu_seqlens,
-                  p.total_tokens, p.Hq, p.Hv, groups, p.gate_dtype, p.param_dtype, ws_T, ws_g};
+    PrepParams pp{static_cast<const __nv_bfloat16 *>(p.q), static_cast<const __nv_bfloat16 *>(p.k), p.A_log,
+                  p.a, p.dt_bias, p.b, p.cu_seqlens, p.total_tokens, p.Hq, p.Hv, groups, p.gate_dtype,
+                  p.param_dtype, ws_T, ws_g, ws_P};
     chunk_prep_kernel<<<dim3(static_cast<unsigned>(chains), groups), kThreads, SMEM_BYTES, stream>>>(pp);
     return cudaGetLastError();
 }

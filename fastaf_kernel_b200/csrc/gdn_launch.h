@@ -2,6 +2,7 @@
 // the kernels.  Arguments are already validated when these are called.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -44,7 +45,8 @@ bool prefill_chunked_supported(const PrefillArgs &p);
 cudaError_t launch_prefill_tc(const PrefillArgs &p, void *workspace, cudaStream_t stream);
 bool prefill_tc_supported(const PrefillArgs &p);
 size_t prefill_tc_workspace_bytes(const PrefillArgs &p);
-cudaError_t launch_chunk_prep(const PrefillArgs &p, float *ws_T, float *ws_g, cudaStream_t stream);
+cudaError_t launch_chunk_prep(const PrefillArgs &p, float *ws_T, __nv_bfloat16 *ws_P, float *ws_g,
+                              cudaStream_t stream);
 // Site of the first bounded device wait of the tcgen05 prefill that gave up (0 = none).
 cudaError_t read_tc_device_error(cudaStream_t stream, int *code, bool clear);
 

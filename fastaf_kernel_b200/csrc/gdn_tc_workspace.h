@@ -8,10 +8,14 @@
 // floor((s0 + L)/64) + n + 1 or later), and every slot is below ceil(T/64) + N,
 // so the workspace is sized from T and N alone, without reading cu_seqlens.
 //
-// Per (slot, v-head):  T = (I + A)^-1 as fp32 [64][64] row-major, zero above the
-// diagonal (16 KB), then, in a second array, the chunk's gate vectors as four
-// fp32 [64] rows: beta, gamma * log2(e), Gamma = exp(gamma), exp(gamma_63 - gamma)
-// (1 KB).  Padding tokens of a partial chunk have beta = 0 and log alpha = 0.
+// Three arrays, each indexed by unit = slot * Hv + v-head:
+//   T  fp32 [64][64] row-major, T = (I + A)^-1 with zeros above the diagonal (16 KB);
+//   P  bf16 [64][64], P[i][j] = exp(gamma_i - gamma_j) q_i.k_j for j <= i, zero above,
+//      stored exactly as the tensor core reads it from shared memory: 128-byte rows
+//      with the 16-byte chunk index XOR-ed by (i & 7) (8 KB);
+//   gates: four fp32 [64] rows: beta, gamma * log2(e), Gamma = exp(gamma),
+//      exp(gamma_63 - gamma) (1 KB).
+// Padding tokens of a partial chunk have beta = 0 and log alpha = 0.
 #pragma once
 
 #include <stdint.h>
@@ -19,14 +23,16 @@
 namespace gdn {
 
 constexpr int64_t kTcTileBytes = 64 * 64 * 4;
+constexpr int64_t kTcPBytes = 64 * 64 * 2;
 constexpr int64_t kTcGateBytes = 4 * 64 * 4;
+constexpr int64_t kTcUnitBytes = kTcTileBytes + kTcPBytes + kTcGateBytes;
 
 __host__ __device__ inline int64_t tc_num_slots(int64_t total_tokens, int64_t num_seqs) {
     return (total_tokens + 63) / 64 + num_seqs;
 }
 
 __host__ __device__ inline int64_t tc_workspace_bytes(int64_t total_tokens, int64_t num_seqs, int Hv) {
-    return tc_num_slots(total_tokens, num_seqs) * Hv * (kTcTileBytes + kTcGateBytes);
+    return tc_num_slots(total_tokens, num_seqs) * Hv * kTcUnitBytes;
 }
 
 __host__ __device__ inline int64_t tc_slot(int64_t s0, int c, int64_t n) {

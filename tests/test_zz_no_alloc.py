@@ -10,7 +10,7 @@ from fastaf_kernel_b200 import workloads as W
 
 DEV = torch.device("cuda", 0)
 CAPACITY = 64 << 20          # bytes of the fixed workspace
-SLOT_BYTES = 17408           # one (chunk, v-head) slot: fp32 T [64][64] + 4 gate vectors
+SLOT_BYTES = 25600           # one (chunk, v-head) slot: fp32 T, bf16 P [64][64], 4 gate vectors
 
 
 def _noalloc(g, out, ns):
