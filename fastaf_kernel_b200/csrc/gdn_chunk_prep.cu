@@ -1,7 +1,7 @@
 // gdn_chunk_prep.cu -- the state-independent half of the chunked prefill, for every
-// chunk of every sequence at once: the chunk's gates and T = (I + A)^-1, written to
-// the workspace of gdn_tc_workspace.h that the tcgen05 chain kernel
-// (gdn_prefill_tc.cu) streams in, together with the chunk's decayed Q K^T tile P.
+// chunk of every sequence at once: the chunk's gates, T = (I + A)^-1 and the decayed
+// Q K^T tile P, written to the workspace of gdn_tc_workspace.h that the tcgen05 chain
+// kernel (gdn_prefill_tc.cu) streams in.
 //
 // For a chunk of tokens i, j = 0..63 (solution/gdn_baseline_torch.py:42-44, 71-87):
 //   log alpha_i = -exp(A_log) softplus(a_i + dt_bias),  beta_i = sigmoid(b_i)
@@ -11,14 +11,19 @@
 // None of it depends on the recurrent state, so all chunks run in parallel here and
 // the chain kernel keeps only the state path on its serial critical path.
 //
-// One CTA per (sequence, v-head, chunk group): the CTA handles chunks g, g + G,
-// g + 2G, ... of its chain, the next chunk's K tile loading while the current one
-// is processed.  K K^T runs on mma.sync (bf16 inputs are exact, fp32 accumulation).
-// T is built block-recursively on mma.sync: the four 16x16 diagonal blocks
-// D_b = (I + A_bb)^-1 by fp32 forward substitution, then
-//   T_10 = -D_1 A_10 D_0,   T_32 = -D_3 A_32 D_2          (T_a, T_b: the 32x32 halves)
-//   T_ba = -T_b A_ba T_a                                    (the 32x32 lower-left block)
-// with every fp32 operand split into bf16 hi + lo (hi*hi + hi*lo + lo*hi).
+// The work of one chunk is a chain of short dependent steps, so the kernel is built
+// for many chunks in flight per SM: CTAs of 4 warps with ~54 KB of shared memory
+// (4 per SM), each handling chunks g, g + G, g + 2G, ... of one (sequence, v-head).
+// Warp w owns rows 16w..16w+15 of the chunk:
+//   * K K^T and Q K^T on mma.sync (bf16 inputs are exact, fp32 accumulation); A stays
+//     in the accumulator registers that computed it, its 16x16 diagonal block also
+//     goes to shared memory in fp32, P goes to the workspace as bf16;
+//   * the four diagonal blocks D_b = (I + A_bb)^-1 by fp32 forward substitution;
+//   * then, block-recursively on mma.sync with every fp32 operand split into bf16
+//     hi + lo (hi*hi + hi*lo + lo*hi):
+//       T_10 = -D_1 A_10 D_0,  T_32 = -D_3 A_32 D_2       (T_a, T_b: the 32x32 halves)
+//       T_ba = -T_b A_ba T_a                              (the 32x32 lower-left block)
+//     where the A blocks come straight from the registers of warps 1, 3 and 2-3.
 #include <cuda_bf16.h>
 
 #include "gdn_chunk_common.cuh"
@@ -33,78 +38,20 @@ namespace {
 using namespace msync;
 
 constexpr int kC = 64;
-constexpr int kThreads = 256;
-constexpr int kLD = 65;                                // fp32 tile row stride (floats)
+constexpr int kThreads = 128;
 
-constexpr uint32_t OFF_K = 0;                          // 2 x bf16 [64][128], 256-byte swizzled rows
-constexpr uint32_t OFF_AH = 2 * 64 * 256;              // bf16 [64][64] A hi/lo (128-byte swizzled rows)
-constexpr uint32_t OFF_AL = OFF_AH + 8192;
-constexpr uint32_t OFF_TH = OFF_AL + 8192;             // bf16 [64][64] T hi/lo
-constexpr uint32_t OFF_TL = OFF_TH + 8192;
-constexpr uint32_t OFF_SH = OFF_TL + 8192;             // bf16 [64][64] intermediate products hi/lo;
-constexpr uint32_t OFF_SL = OFF_SH + 8192;             // before them, the Q tile [64][128] (16 KB)
-constexpr uint32_t OFF_AD = OFF_SL + 8192;             // fp32 diagonal blocks of A: 4 x [16][17]
-constexpr uint32_t OFF_T = OFF_AD + 4 * 16 * 17 * 4;   // fp32 T [64][65]
-constexpr uint32_t OFF_GATE = OFF_T + 64 * kLD * 4;    // beta, gamma*log2(e), Gamma, decay-to-end
+// Shared memory (bytes).  The K tile becomes the fp32 T tile once K K^T and Q K^T are
+// done; the Q tile becomes the hi/lo tiles of the intermediate products.
+constexpr uint32_t OFF_K = 0;                       // bf16 [64][128], 256-byte swizzled rows
+constexpr uint32_t OFF_TF = 0;                      // fp32 T [64][64] row-major (over K)
+constexpr uint32_t OFF_Q = 16384;                   // bf16 [64][128], 256-byte swizzled rows
+constexpr uint32_t OFF_SH = 16384;                  // bf16 [64][64] intermediate products hi/lo (over Q)
+constexpr uint32_t OFF_SL = 24576;
+constexpr uint32_t OFF_TH = 32768;                  // bf16 [64][64] T hi/lo, 128-byte swizzled rows
+constexpr uint32_t OFF_TL = 40960;
+constexpr uint32_t OFF_AD = 49152;                  // fp32 diagonal blocks of A: 4 x [16][17]
+constexpr uint32_t OFF_GATE = OFF_AD + 4 * 16 * 17 * 4;   // beta, gamma*log2(e), Gamma, decay-to-end
 constexpr uint32_t SMEM_BYTES = OFF_GATE + 4 * 64 * 4;
-
-// acc (16 x 16 as two m16n8 tiles) += X[xr.., xc..xc+16ks) * Y[yr..yr+16ks, yc..yc+16) with
-// X and Y bf16 hi/lo tiles [64][64]; hi*hi + hi*lo + lo*hi carries ~fp32 accuracy.
-__device__ __forceinline__ void prod16(float (&acc)[2][4], uint32_t Xh, uint32_t Xl, uint32_t Yh,
-                                       uint32_t Yl, int xr, int xc, int yr, int yc, int ks, int lane) {
-    for (int s = 0; s < ks; ++s) {
-        uint32_t ah[4], al[4], bh[4], bl[4];
-        ldsm_x4(ah, a_addr<128>(Xh, xr, xc + 16 * s, lane));
-        ldsm_x4(al, a_addr<128>(Xl, xr, xc + 16 * s, lane));
-        ldsm_x4_t(bh, b_addr_kn<128>(Yh, yc, yr + 16 * s, lane));
-        ldsm_x4_t(bl, b_addr_kn<128>(Yl, yc, yr + 16 * s, lane));
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-            mma16816(acc[nt], ah, bh[2 * nt], bh[2 * nt + 1]);
-            mma16816(acc[nt], ah, bl[2 * nt], bl[2 * nt + 1]);
-            mma16816(acc[nt], al, bh[2 * nt], bh[2 * nt + 1]);
-        }
-    }
-}
-
-// Store a 16x16 accumulator block (rows r0.., cols c0..), times `sgn`, as bf16 hi/lo
-// into tiles Hh/Hl and, when F != nullptr, as fp32 into F (row stride kLD).
-__device__ __forceinline__ void store16(const float (&acc)[2][4], float sgn, uint8_t *Hh, uint8_t *Hl,
-                                        float *F, int r0, int c0, int lane) {
-    const int g = lane >> 2, t4 = lane & 3;
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-            const int row = r0 + g + 8 * hf, col = c0 + nt * 8 + 2 * t4;
-            const float v0 = sgn * acc[nt][2 * hf], v1 = sgn * acc[nt][2 * hf + 1];
-            float h0, l0, h1, l1;
-            split_bf16(v0, h0, l0);
-            split_bf16(v1, h1, l1);
-            *reinterpret_cast<uint32_t *>(Hh + swz<128>(row, col)) = pack_bf16x2(h0, h1);
-            *reinterpret_cast<uint32_t *>(Hl + swz<128>(row, col)) = pack_bf16x2(l0, l1);
-            if (F) {
-                F[row * kLD + col] = v0;
-                F[row * kLD + col + 1] = v1;
-            }
-        }
-}
-
-// A [64][128] bf16 tile (rows t0.., head hq) into 256-byte swizzled rows; rows past T
-// read as zero.  One cp.async group.
-__device__ __forceinline__ void load_k_tile(uint32_t sK, const __nv_bfloat16 *k, int64_t T, int Hq, int hq,
-                                            int64_t t0, int tid) {
-#pragma unroll
-    for (int u = 0; u < (64 * 16) / 256; ++u) {
-        const int idx = tid + u * 256;
-        const int j = idx >> 4, ch = idx & 15;
-        const int64_t t = t0 + j;
-        const bool ok = t < T;
-        cp_async16(sK + j * 256 + ((ch ^ (j & 7)) << 4), k + ((ok ? t : 0) * Hq + hq) * kHeadDim + ch * 8,
-                   ok ? 16 : 0);
-    }
-    cp_async_commit();
-}
 
 struct PrepParams {
     const __nv_bfloat16 *q, *k;
@@ -117,7 +64,80 @@ struct PrepParams {
     __nv_bfloat16 *ws_P;
 };
 
-__global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(const PrepParams p) {
+// [64][128] bf16 rows t0.. of head hh into 256-byte swizzled rows; rows past T read
+// as zero (tokens past the sequence end only meet beta = 0 rows and j >= i columns).
+__device__ __forceinline__ void load_tile(uint32_t dst, const __nv_bfloat16 *src, int64_t T, int H, int hh,
+                                          int64_t t0, int tid) {
+#pragma unroll
+    for (int u = 0; u < (64 * 16) / kThreads; ++u) {
+        const int idx = tid + u * kThreads;
+        const int j = idx >> 4, ch = idx & 15;
+        const int64_t t = t0 + j;
+        const bool ok = t < T;
+        cp_async16(dst + j * 256 + ((ch ^ (j & 7)) << 4), src + ((ok ? t : 0) * H + hh) * kHeadDim + ch * 8,
+                   ok ? 16 : 0);
+    }
+}
+
+// acc (16 x 8*NT) += X[16 rows][16 KS] . Y, X as per-k-step hi/lo A fragments in
+// registers, Y (k rows, n columns) from bf16 hi/lo tiles [64][64] via ldmatrix.trans;
+// hi*hi + hi*lo + lo*hi.
+template <int KS, int NT>
+__device__ __forceinline__ void prod_rf(float (&acc)[NT][4], const uint32_t (&xh)[KS][4],
+                                        const uint32_t (&xl)[KS][4], uint32_t Yh, uint32_t Yl, int yr,
+                                        int yc, int lane) {
+#pragma unroll
+    for (int s = 0; s < KS; ++s)
+#pragma unroll
+        for (int np = 0; np < NT / 2; ++np) {
+            uint32_t bh[4], bl[4];
+            ldsm_x4_t(bh, b_addr_kn<128>(Yh, yc + 16 * np, yr + 16 * s, lane));
+            ldsm_x4_t(bl, b_addr_kn<128>(Yl, yc + 16 * np, yr + 16 * s, lane));
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                mma16816(acc[2 * np + u], xh[s], bh[2 * u], bh[2 * u + 1]);
+                mma16816(acc[2 * np + u], xh[s], bl[2 * u], bl[2 * u + 1]);
+                mma16816(acc[2 * np + u], xl[s], bh[2 * u], bh[2 * u + 1]);
+            }
+        }
+}
+
+// X fragments (rows xr.., k columns xc.. xc + 16 KS) from bf16 hi/lo tiles [64][64].
+template <int KS>
+__device__ __forceinline__ void load_frags(uint32_t (&xh)[KS][4], uint32_t (&xl)[KS][4], uint32_t Xh,
+                                           uint32_t Xl, int xr, int xc, int lane) {
+#pragma unroll
+    for (int s = 0; s < KS; ++s) {
+        ldsm_x4(xh[s], a_addr<128>(Xh, xr, xc + 16 * s, lane));
+        ldsm_x4(xl[s], a_addr<128>(Xl, xr, xc + 16 * s, lane));
+    }
+}
+
+// Store a 16 x 8*NT accumulator block (rows r0.., cols c0..), times `sgn`, as bf16 hi/lo
+// into tiles Hh/Hl (when Hh != nullptr) and as fp32 into the row-major [64][64] tile F
+// (when F != nullptr).
+template <int NT>
+__device__ __forceinline__ void store_block(const float (&acc)[NT][4], float sgn, uint8_t *Hh, uint8_t *Hl,
+                                            float *F, int r0, int c0, int lane) {
+    const int g = lane >> 2, t4 = lane & 3;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+            const int row = r0 + g + 8 * hf, col = c0 + nt * 8 + 2 * t4;
+            const float v0 = sgn * acc[nt][2 * hf], v1 = sgn * acc[nt][2 * hf + 1];
+            if (Hh) {
+                float h0, l0, h1, l1;
+                split_bf16(v0, h0, l0);
+                split_bf16(v1, h1, l1);
+                *reinterpret_cast<uint32_t *>(Hh + swz<128>(row, col)) = pack_bf16x2(h0, h1);
+                *reinterpret_cast<uint32_t *>(Hl + swz<128>(row, col)) = pack_bf16x2(l0, l1);
+            }
+            if (F) *reinterpret_cast<float2 *>(F + row * 64 + col) = make_float2(v0, v1);
+        }
+}
+
+__global__ void __launch_bounds__(kThreads, 4) chunk_prep_kernel(const PrepParams p) {
     extern __shared__ __align__(1024) uint8_t sm[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t4 = lane & 3;
@@ -129,45 +149,50 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(const PrepParam
     s0 = s0 < 0 ? 0 : (s0 > p.T ? p.T : s0);
     s1 = s1 < s0 ? s0 : (s1 > p.T ? p.T : s1);
     const int nch = static_cast<int>((s1 - s0 + kC - 1) / kC);
+    if (static_cast<int>(blockIdx.y) >= nch) return;
 
     const uint32_t sbase = smem_addr(sm);
     float *A_d = reinterpret_cast<float *>(sm + OFF_AD);
-    float *T_f = reinterpret_cast<float *>(sm + OFF_T);
+    float *T_f = reinterpret_cast<float *>(sm + OFF_TF);
     float *g_beta = reinterpret_cast<float *>(sm + OFF_GATE);
     float *g_gam2 = g_beta + 64, *g_Gam = g_beta + 128, *g_dec = g_beta + 192;
     const float exp_A = expf(load_scalar(p.A_log, h, p.param_dtype));
     const float dtb = load_scalar(p.dt_bias, h, p.param_dtype);
+    const uint32_t Th = sbase + OFF_TH, Tl = sbase + OFF_TL, Sh = sbase + OFF_SH, Sl = sbase + OFF_SL;
+    const int r0 = 16 * warp;    // this warp's rows of the chunk
 
-    // Tokens past T read as zero; tokens past the sequence end only meet beta = 0
-    // rows and j >= i columns of A.
-    int c = blockIdx.y;
-    if (c < nch) load_k_tile(sbase + OFF_K, p.k, p.T, p.Hq, hq, s0 + static_cast<int64_t>(c) * kC, tid);
-    for (int it = 0; c < nch; c += p.groups, ++it) {
+    // Warp 0 keeps the next chunk's gate inputs in registers (loaded a chunk ahead).
+    float ga[2] = {0.f, 0.f}, gb[2] = {0.f, 0.f};
+    auto fetch_gates = [&](int cc) {
+        const int64_t tb = s0 + static_cast<int64_t>(cc) * kC;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int64_t t = tb + lane + 32 * u;
+            if (t < s1) {
+                ga[u] = load_scalar(p.a, t * p.Hv + h, p.gate_dtype);
+                gb[u] = load_scalar(p.b, t * p.Hv + h, p.gate_dtype);
+            }
+        }
+    };
+    if (warp == 0) fetch_gates(blockIdx.y);
+
+    for (int c = blockIdx.y; c < nch; c += p.groups) {
         const int64_t t0 = s0 + static_cast<int64_t>(c) * kC;
         const int nt = static_cast<int>(s1 - t0 < kC ? s1 - t0 : kC);
-        const uint32_t sK = sbase + OFF_K + (it & 1) * (64 * 256);
-        // This chunk's Q tile into the intermediate-product tiles (free until the products),
-        // then the next chunk's K tile into the other K buffer.
-        load_k_tile(sbase + OFF_SH, p.q, p.T, p.Hq, hq, t0, tid);
-        const int cn = c + p.groups;
-        if (cn < nch)
-            load_k_tile(sbase + OFF_K + ((it + 1) & 1) * (64 * 256), p.k, p.T, p.Hq, hq,
-                        s0 + static_cast<int64_t>(cn) * kC, tid);
+        load_tile(sbase + OFF_K, p.k, p.T, p.Hq, hq, t0, tid);
+        load_tile(sbase + OFF_Q, p.q, p.T, p.Hq, hq, t0, tid);
+        cp_async_commit();
 
-        // Gates (warp 0) while the tiles are in flight.
+        // Gates (warp 0), then the next chunk's inputs.
         if (warp == 0) {
             float lg[2], bt[2];
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
-                const int i = lane + 32 * u;
-                lg[u] = 0.0f;
-                bt[u] = 0.0f;
-                if (i < nt) {
-                    const int64_t gi = (t0 + i) * p.Hv + h;
-                    lg[u] = log_decay(exp_A, load_scalar(p.a, gi, p.gate_dtype), dtb);
-                    bt[u] = sigmoid_f(load_scalar(p.b, gi, p.gate_dtype));
-                }
+                const bool live = lane + 32 * u < nt;
+                lg[u] = live ? log_decay(exp_A, ga[u], dtb) : 0.0f;
+                bt[u] = live ? sigmoid_f(gb[u]) : 0.0f;
             }
+            if (c + p.groups < nch) fetch_gates(c + p.groups);
             float x0 = lg[0], x1 = lg[1];
 #pragma unroll
             for (int off = 1; off < 32; off <<= 1) {
@@ -183,59 +208,86 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(const PrepParam
             g_Gam[lane] = expf(x0); g_Gam[lane + 32] = expf(x1);
             g_dec[lane] = expf(xC - x0); g_dec[lane + 32] = expf(xC - x1);
         }
-        // cp.async groups, oldest first: this chunk's K, its Q, [the next chunk's K].
-        if (cn < nch) cp_async_wait<2>(); else cp_async_wait<1>();
+        cp_async_wait<0>();
         __syncthreads();
 
-        // K K^T: warp w computes rows 16*(w&3).. and columns 32*(w>>2).. on mma.sync;
-        // A[i][j] = beta_i exp(gamma_i - gamma_j) k_i.k_j for j < i (zero elsewhere) goes
-        // to the A hi/lo tiles, its diagonal 16x16 blocks also to A_d in fp32.
+        // K K^T rows r0..r0+15 (columns right of the diagonal block are zero in A and
+        // skipped); A = beta_i exp(gamma_i - gamma_j) k_i.k_j for j < i stays in these
+        // registers, its diagonal block also goes to A_d (fp32).
+        float A[8][4];
         {
-            const int r0 = (warp & 3) * 16, c0 = (warp >> 2) * 32;
-            float acc[4][4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
+            for (int i = 0; i < 8; ++i) A[i][0] = A[i][1] = A[i][2] = A[i][3] = 0.0f;
+            const uint32_t sK = sbase + OFF_K;
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) {
                 uint32_t af[4];
                 ldsm_x4(af, a_addr<256>(sK, r0, kk * 16, lane));
 #pragma unroll
-                for (int np = 0; np < 2; ++np) {
+                for (int np = 0; np < 4; ++np) {
+                    if (16 * np > r0) continue;
                     uint32_t bf[4];
-                    ldsm_x4(bf, b_addr_nk<256>(sK, c0 + np * 16, kk * 16, lane));
-                    mma16816(acc[2 * np], af, bf[0], bf[1]);
-                    mma16816(acc[2 * np + 1], af, bf[2], bf[3]);
+                    ldsm_x4(bf, b_addr_nk<256>(sK, np * 16, kk * 16, lane));
+                    mma16816(A[2 * np], af, bf[0], bf[1]);
+                    mma16816(A[2 * np + 1], af, bf[2], bf[3]);
                 }
             }
-            const int blk = warp & 3;
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                const int i = r0 + g + 8 * half;
+            for (int hf = 0; hf < 2; ++hf) {
+                const int i = r0 + g + 8 * hf;
                 const float gi = g_gam2[i], bi = g_beta[i];
 #pragma unroll
-                for (int ntl = 0; ntl < 4; ++ntl) {
-                    const int j = c0 + ntl * 8 + 2 * t4;
-                    float v[2];
+                for (int ntl = 0; ntl < 8; ++ntl) {
 #pragma unroll
-                    for (int u = 0; u < 2; ++u)
-                        v[u] = j + u < i ? bi * exp2f(gi - g_gam2[j + u]) * acc[ntl][2 * half + u] : 0.0f;
-                    float h0, l0, h1, l1;
-                    split_bf16(v[0], h0, l0);
-                    split_bf16(v[1], h1, l1);
-                    *reinterpret_cast<uint32_t *>(sm + OFF_AH + swz<128>(i, j)) = pack_bf16x2(h0, h1);
-                    *reinterpret_cast<uint32_t *>(sm + OFF_AL + swz<128>(i, j)) = pack_bf16x2(l0, l1);
-                    if ((j >> 4) == blk) {
-                        A_d[(blk * 16 + (i & 15)) * 17 + (j & 15)] = v[0];
-                        A_d[(blk * 16 + (i & 15)) * 17 + (j & 15) + 1] = v[1];
+                    for (int u = 0; u < 2; ++u) {
+                        const int j = ntl * 8 + 2 * t4 + u;
+                        const float a = j < i ? bi * exp2f(gi - g_gam2[j]) * A[ntl][2 * hf + u] : 0.0f;
+                        A[ntl][2 * hf + u] = a;
+                        if ((j >> 4) == warp) A_d[(16 * warp + (i & 15)) * 17 + (j & 15)] = a;
                     }
                 }
             }
         }
-        __syncthreads();
+        // Q K^T rows r0.. -> P = exp(gamma_i - gamma_j) q_i.k_j for j <= i, to the workspace
+        // as bf16 in the swizzled layout the chain kernel's tensor core reads.
+        const int64_t unit = tc_slot(s0, c, n) * p.Hv + h;
+        {
+            float acc[8][4];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
+            const uint32_t sK = sbase + OFF_K, sQ = sbase + OFF_Q;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                uint32_t af[4];
+                ldsm_x4(af, a_addr<256>(sQ, r0, kk * 16, lane));
+#pragma unroll
+                for (int np = 0; np < 4; ++np) {
+                    if (16 * np > r0) continue;
+                    uint32_t bf[4];
+                    ldsm_x4(bf, b_addr_nk<256>(sK, np * 16, kk * 16, lane));
+                    mma16816(acc[2 * np], af, bf[0], bf[1]);
+                    mma16816(acc[2 * np + 1], af, bf[2], bf[3]);
+                }
+            }
+            uint8_t *dP = reinterpret_cast<uint8_t *>(p.ws_P) + unit * kTcPBytes;
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                const int i = r0 + g + 8 * hf;
+                const float gi = g_gam2[i];
+#pragma unroll
+                for (int ntl = 0; ntl < 8; ++ntl) {
+                    const int j = ntl * 8 + 2 * t4;
+                    const float p0 = j <= i ? exp2f(gi - g_gam2[j]) * acc[ntl][2 * hf] : 0.0f;
+                    const float p1 = j + 1 <= i ? exp2f(gi - g_gam2[j + 1]) * acc[ntl][2 * hf + 1] : 0.0f;
+                    *reinterpret_cast<uint32_t *>(dP + swz<128>(i, j)) = pack_bf16x2(p0, p1);
+                }
+            }
+        }
+        __syncthreads();   // A_d complete; the K and Q tiles are dead from here on
 
-        // D_b = (I + A_bb)^-1: thread (block o, column cc) of threads 0-63 solves column
-        // cc by forward substitution (two partial sums per row).  Threads 64-127 zero
-        // the upper off-diagonal blocks of T_a and T_b in the T hi/lo tiles.
+        // D_b = (I + A_bb)^-1 (threads 0-63: block ob, column cc, forward substitution with
+        // two partial sums per row) -> T hi/lo tiles and T_f; threads 64-127 zero the upper
+        // off-diagonal blocks of T_a and T_b in the T hi/lo tiles.
         if (tid < 64) {
             const int ob = tid >> 4, cc = tid & 15, o = ob * 16;
             const float *Ab = A_d + ob * 16 * 17;
@@ -254,11 +306,11 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(const PrepParam
             for (int r = 0; r < 16; ++r) {
                 float hi, lo;
                 split_bf16(x[r], hi, lo);
-                reinterpret_cast<__nv_bfloat16 *>(sm + OFF_TH + swz<128>(o + r, o + cc))[0] = __float2bfloat16_rn(hi);
-                reinterpret_cast<__nv_bfloat16 *>(sm + OFF_TL + swz<128>(o + r, o + cc))[0] = __float2bfloat16_rn(lo);
-                T_f[(o + r) * kLD + o + cc] = x[r];
+                *reinterpret_cast<__nv_bfloat16 *>(sm + OFF_TH + swz<128>(o + r, o + cc)) = __float2bfloat16_rn(hi);
+                *reinterpret_cast<__nv_bfloat16 *>(sm + OFF_TL + swz<128>(o + r, o + cc)) = __float2bfloat16_rn(lo);
+                T_f[(o + r) * 64 + o + cc] = x[r];
             }
-        } else if (tid < 128) {
+        } else {
             const int e = tid - 64, r = e >> 2, q = e & 3;     // 16 rows x 4 quads of 4 columns
 #pragma unroll
             for (int blkz = 0; blkz < 2; ++blkz) {
@@ -269,84 +321,44 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(const PrepParam
         }
         __syncthreads();
 
-        // Q K^T on mma.sync, same warp tiling as K K^T; P (bf16, swizzled) straight to the workspace.
-        const int64_t unit = tc_slot(s0, c, n) * p.Hv + h;
-        if (cn < nch) cp_async_wait<1>(); else cp_async_wait<0>();
-        __syncthreads();
-        {
-            const uint32_t sQ = sbase + OFF_SH;
-            const int r0 = (warp & 3) * 16, c0 = (warp >> 2) * 32;
-            float acc[4][4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-                uint32_t af[4];
-                ldsm_x4(af, a_addr<256>(sQ, r0, kk * 16, lane));
-#pragma unroll
-                for (int np = 0; np < 2; ++np) {
-                    uint32_t bf[4];
-                    ldsm_x4(bf, b_addr_nk<256>(sK, c0 + np * 16, kk * 16, lane));
-                    mma16816(acc[2 * np], af, bf[0], bf[1]);
-                    mma16816(acc[2 * np + 1], af, bf[2], bf[3]);
-                }
-            }
-            uint8_t *dP = reinterpret_cast<uint8_t *>(p.ws_P) + unit * kTcPBytes;
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                const int i = r0 + g + 8 * half;
-                const float gi = g_gam2[i];
-#pragma unroll
-                for (int ntl = 0; ntl < 4; ++ntl) {
-                    const int j = c0 + ntl * 8 + 2 * t4;
-                    const float p0 = j <= i ? exp2f(gi - g_gam2[j]) * acc[ntl][2 * half] : 0.0f;
-                    const float p1 = j + 1 <= i ? exp2f(gi - g_gam2[j + 1]) * acc[ntl][2 * half + 1] : 0.0f;
-                    *reinterpret_cast<uint32_t *>(dP + swz<128>(i, j)) = pack_bf16x2(p0, p1);
-                }
-            }
-        }
-        __syncthreads();   // the Q tile is dead; the products below reuse its space
-
-        const uint32_t Ah = sbase + OFF_AH, Al = sbase + OFF_AL, Th = sbase + OFF_TH, Tl = sbase + OFF_TL;
-        const uint32_t Sh = sbase + OFF_SH, Sl = sbase + OFF_SL;
-        // M_10 = A_10 D_0 (warp 0), M_32 = A_32 D_2 (warp 1)
-        if (warp < 2) {
-            const int o = warp * 32;
+        // M_10 = A_10 D_0 (warp 1), M_32 = A_32 D_2 (warp 3); A blocks from registers.
+        if (warp & 1) {
+            const int o = warp == 1 ? 0 : 32;       // column block of A_10 / A_32
+            uint32_t xh[1][4], xl[1][4];
+            if (warp == 1) acc_to_a_split(A[0], A[1], xh[0], xl[0]);   // static indices keep A in registers
+            else acc_to_a_split(A[4], A[5], xh[0], xl[0]);
             float acc[2][4] = {};
-            prod16(acc, Ah, Al, Th, Tl, o + 16, o, o, o, 1, lane);
-            store16(acc, 1.0f, sm + OFF_SH, sm + OFF_SL, nullptr, o + 16, o, lane);
+            prod_rf<1, 2>(acc, xh, xl, Th, Tl, o, o, lane);
+            store_block<2>(acc, 1.0f, sm + OFF_SH, sm + OFF_SL, nullptr, r0, o, lane);
         }
         __syncthreads();
-        // T_10 = -D_1 M_10 (warp 0), T_32 = -D_3 M_32 (warp 1)
-        if (warp < 2) {
-            const int o = warp * 32;
+        // T_10 = -D_1 M_10 (warp 1), T_32 = -D_3 M_32 (warp 3)
+        if (warp & 1) {
+            const int o = warp == 1 ? 0 : 32;
+            uint32_t xh[1][4], xl[1][4];
+            load_frags<1>(xh, xl, Th, Tl, r0, r0, lane);
             float acc[2][4] = {};
-            prod16(acc, Th, Tl, Sh, Sl, o + 16, o + 16, o + 16, o, 1, lane);
-            store16(acc, -1.0f, sm + OFF_TH, sm + OFF_TL, T_f, o + 16, o, lane);
+            prod_rf<1, 2>(acc, xh, xl, Sh, Sl, r0, o, lane);
+            store_block<2>(acc, -1.0f, sm + OFF_TH, sm + OFF_TL, T_f, r0, o, lane);
         }
         __syncthreads();
-        // M_ba = A[32..64)[0..32) T_a (warps 0-3, one 16x16 block each)
-        if (warp < 4) {
-            const int rb = warp >> 1, cb = warp & 1;
-            float acc[2][4] = {};
-            prod16(acc, Ah, Al, Th, Tl, 32 + 16 * rb, 0, 0, 16 * cb, 2, lane);
-            store16(acc, 1.0f, sm + OFF_SH, sm + OFF_SL, nullptr, 32 + 16 * rb, 16 * cb, lane);
+        // M_ba = A[32..64)[0..32) T_a (warps 2, 3); A from registers.
+        if (warp >= 2) {
+            uint32_t xh[2][4], xl[2][4];
+            acc_to_a_split(A[0], A[1], xh[0], xl[0]);
+            acc_to_a_split(A[2], A[3], xh[1], xl[1]);
+            float acc[4][4] = {};
+            prod_rf<2, 4>(acc, xh, xl, Th, Tl, 0, 0, lane);
+            store_block<4>(acc, 1.0f, sm + OFF_SH, sm + OFF_SL, nullptr, r0, 0, lane);
         }
         __syncthreads();
-        // T_ba = -T_b M_ba
-        if (warp < 4) {
-            const int rb = warp >> 1, cb = warp & 1;
-            float acc[2][4] = {};
-            prod16(acc, Th, Tl, Sh, Sl, 32 + 16 * rb, 32, 32, 16 * cb, 2, lane);
-            const int gg = lane >> 2, tt = lane & 3;
-#pragma unroll
-            for (int ntl = 0; ntl < 2; ++ntl)
-#pragma unroll
-                for (int hf = 0; hf < 2; ++hf) {
-                    const int row = 32 + 16 * rb + gg + 8 * hf, col = 16 * cb + ntl * 8 + 2 * tt;
-                    T_f[row * kLD + col] = -acc[ntl][2 * hf];
-                    T_f[row * kLD + col + 1] = -acc[ntl][2 * hf + 1];
-                }
+        // T_ba = -T_b M_ba (warps 2, 3)
+        if (warp >= 2) {
+            uint32_t xh[2][4], xl[2][4];
+            load_frags<2>(xh, xl, Th, Tl, r0, 32, lane);
+            float acc[4][4] = {};
+            prod_rf<2, 4>(acc, xh, xl, Sh, Sl, 32, 0, lane);
+            store_block<4>(acc, -1.0f, nullptr, nullptr, T_f, r0, 0, lane);
         }
         __syncthreads();
 
@@ -356,23 +368,25 @@ __global__ void __launch_bounds__(kThreads, 2) chunk_prep_kernel(const PrepParam
         for (int u = 0; u < (64 * 16) / kThreads; ++u) {
             const int idx = tid + u * kThreads;
             const int i = idx >> 4, j = (idx & 15) * 4;
+            const float4 t = *reinterpret_cast<const float4 *>(T_f + i * 64 + j);
             float4 val;
-            val.x = j <= i ? T_f[i * kLD + j] : 0.0f;
-            val.y = j + 1 <= i ? T_f[i * kLD + j + 1] : 0.0f;
-            val.z = j + 2 <= i ? T_f[i * kLD + j + 2] : 0.0f;
-            val.w = j + 3 <= i ? T_f[i * kLD + j + 3] : 0.0f;
+            val.x = j <= i ? t.x : 0.0f;
+            val.y = j + 1 <= i ? t.y : 0.0f;
+            val.z = j + 2 <= i ? t.z : 0.0f;
+            val.w = j + 3 <= i ? t.w : 0.0f;
             *reinterpret_cast<float4 *>(dT + i * 64 + j) = val;
         }
         p.ws_g[unit * (kTcGateBytes / 4) + tid] = g_beta[tid];
-        __syncthreads();   // the next chunk reuses every shared buffer
+        p.ws_g[unit * (kTcGateBytes / 4) + 128 + tid] = g_beta[128 + tid];
+        __syncthreads();   // the next chunk's copies overwrite T_f and the tiles
     }
 }
 
 }  // namespace
 
 int prep_groups(int64_t chains) {
-    // Enough CTAs for a few waves of 148 SMs x 2 resident CTAs.
-    const int64_t want = 4 * 148 * 2;
+    // Enough CTAs for several waves of 148 SMs x 4 resident CTAs.
+    const int64_t want = 8 * 148 * 4;
     int64_t gsz = (want + chains - 1) / chains;
     return static_cast<int>(gsz < 1 ? 1 : (gsz > 64 ? 64 : gsz));
 }

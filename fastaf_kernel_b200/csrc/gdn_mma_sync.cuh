@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include "gdn_chunk_common.cuh"
+#include "gdn_common.cuh"
 
 namespace gdn {
 namespace msync {
@@ -67,6 +68,28 @@ template <int kRowBytes>
 __device__ __forceinline__ uint32_t b_addr_kn(uint32_t base, int n0, int k0, int lane) {
     const int q = lane >> 3;
     return base + swz<kRowBytes>(k0 + (lane & 7) + ((q & 1) << 3), n0 + ((q >> 1) << 3));
+}
+
+// A fragment for k-step kk built from fp32 accumulators of n-tiles 2kk, 2kk+1
+// (the accumulator's columns become the next product's K dimension).
+__device__ __forceinline__ void acc_to_a_bf16(const float (&c0)[4], const float (&c1)[4],
+                                              uint32_t (&a)[4]) {
+    a[0] = pack_bf16x2(c0[0], c0[1]);
+    a[1] = pack_bf16x2(c0[2], c0[3]);
+    a[2] = pack_bf16x2(c1[0], c1[1]);
+    a[3] = pack_bf16x2(c1[2], c1[3]);
+}
+__device__ __forceinline__ void acc_to_a_split(const float (&c0)[4], const float (&c1)[4],
+                                               uint32_t (&hi)[4], uint32_t (&lo)[4]) {
+    float h[8], l[8];
+    const float v[8] = {c0[0], c0[1], c0[2], c0[3], c1[0], c1[1], c1[2], c1[3]};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) split_bf16(v[e], h[e], l[e]);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        hi[e] = pack_bf16x2(h[2 * e], h[2 * e + 1]);
+        lo[e] = pack_bf16x2(l[2 * e], l[2 * e + 1]);
+    }
 }
 
 }  // namespace msync
