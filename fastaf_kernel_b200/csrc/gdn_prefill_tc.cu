@@ -17,15 +17,18 @@
 // partial chunk have beta = 0 and log alpha = 0.  Every product with an fp32 operand
 // (S0, T, W, the decayed delta) splits it into bf16 hi + lo.
 //
-// One CTA per (sequence, v-head) chain, 13 warps in three roles that hand chunks to
+// One CTA per (sequence, v-head) chain, 14 warps in four roles that hand chunks to
 // each other through mbarriers, so the next chunk's state-independent products run
 // while the current chunk's state update is on the tensor core:
-//   warp 0      allocates all 512 TMEM columns; lane 0 issues every TMA copy and every
-//               MMA, each batch as soon as its inputs are ready, state path first
+//   warp 0      allocates all 512 TMEM columns; lane 0 issues every MMA, each batch as
+//               soon as its inputs are ready, state path first
+//   warp 13     lane 0 issues the copies of each chunk (TMA tiles, bulk P and gates) as
+//               soon as the chunk two back has left its stage
 //   warps 1-4   prep (one per TMEM lane quadrant): T' = T diag(beta), T'' = T diag(beta
-//               Gamma) and diag(Gamma) Q tiles, then -W from W^T in TMEM
+//               Gamma) and diag(Gamma) Q tiles, -W from W^T in TMEM, then the previous
+//               chunk's output rows from O^T in TMEM
 //   warps 5-12  state path, two halves of four warps: S -> hi/lo split and decay, the
-//               innovation split, the output rows
+//               innovation split
 // The fp32 state lives in TMEM columns [0,128) for the whole sequence.
 //
 // Every wait is bounded (about 2 s).  A wait that gives up records its site in
@@ -51,7 +54,7 @@ namespace {
 using namespace sm100;
 
 constexpr int kC = 64;
-constexpr int kThreads = 416;   // warp 0: TMA + MMA issue; warps 1-4: prep; warps 5-12: state (two halves)
+constexpr int kThreads = 448;   // warp 0: MMA issue; warps 1-4: prep; warps 5-12: state (two halves); warp 13: copies
 
 // Shared memory map (bytes from the 1024-aligned dynamic base).
 constexpr uint32_t OFF_KQ = 0;              // 2 stages x 32 KB: [K_h0 | Q_h0 | K_h1 | Q_h1]
@@ -67,7 +70,7 @@ constexpr uint32_t OFF_T2H = 160 * 1024;
 constexpr uint32_t OFF_T2L = 168 * 1024;
 constexpr uint32_t OFF_WH = 176 * 1024;     // 16 KB each: -W hi/lo, MN-major [k][i]
 constexpr uint32_t OFF_WL = 192 * 1024;
-constexpr uint32_t OFF_O = 208 * 1024;      // 2 x 8 KB: bf16 [32][128] output staging, one per state half
+constexpr uint32_t OFF_O = 208 * 1024;      // 16 KB: bf16 [64][128] output staging
 constexpr uint32_t OFF_GST = 224 * 1024;    // 2 stages x 1 KB: beta, gamma*log2(e), Gamma, decay-to-end
 constexpr uint32_t SMEM_BYTES = 226 * 1024;
 constexpr uint32_t kStageTx = 6 * 8192 + kTcPBytes + kTcGateBytes;
@@ -85,6 +88,7 @@ constexpr uint32_t TM_O = 448;    // [448,512) (Gamma Q S^T)^T, then O^T
 
 enum WaitSite { kWaitTma = 1, kWaitWU = 3, kWaitD = 4, kWaitS = 5, kWaitTT = 6,
                 kWaitW = 7, kWaitSS = 8, kWaitDS = 9, kWaitT = 10, kWaitIssue = 11 };
+// (output reads O^T of chunk c before the delta batch of chunk c + 1 overwrites it)
 
 struct TcParams {
     const float *state;
@@ -99,7 +103,7 @@ struct TcParams {
 };
 
 struct Bars {
-    uint64_t tma[2], wu, d, s, tt, w, ss, ds, t, free_[2];
+    uint64_t tma[2], wu, d, s, tt, w, ss, ds, t, free_[2], oread;
 };
 
 __device__ __forceinline__ void issue_chunk(const CUtensorMap *qmap, const CUtensorMap *kmap,
@@ -178,6 +182,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
     const uint32_t b_ss = smem_u32(&bars.ss), b_ds = smem_u32(&bars.ds), b_t = smem_u32(&bars.t);
     // free[b]: chunk c's S-update batch (the last reader of stage c & 1 and P buffer c & 1) is done
     const uint32_t b_free0 = smem_u32(&bars.free_[0]), b_free1 = smem_u32(&bars.free_[1]);
+    const uint32_t b_oread = smem_u32(&bars.oread);   // the prep warps have read O^T of a chunk
     float *dst_state = p.new_state + chain * kHeadDim * kHeadDim;
 
     if (warp == 0) {
@@ -194,6 +199,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             mbar_init(b_t, 1);
             mbar_init(b_free0, 1);
             mbar_init(b_free1, 1);
+            mbar_init(b_oread, 4);
             abort_flag = 0;
             fence_mbar_init();
         }
@@ -211,17 +217,9 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         for (int i = tid; i < kHeadDim * kHeadDim / 4; i += kThreads)
             reinterpret_cast<float4 *>(dst_state)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     } else if (warp == 0) {
-        // ------------------------------------------------------------ TMA + MMA issue
+        // ------------------------------------------------------------ MMA issue
         if (lane == 0) {
-            int tma_issued = 0, tma_waited = 0;
             int n_wu = 0, n_d = 0, n_s = 0;
-            for (int c = 0; c < 2 && c < nch; ++c) {
-                const int64_t unit = tc_slot(s0, c, n) * p.Hv + h;
-                issue_chunk(&qmap, &kmap, &vmap, sbase, c, p.ws_P + unit * (kTcPBytes / 2),
-                            p.ws_g + unit * (kTcGateBytes / 4), c ? b_tma1 : b_tma0,
-                            static_cast<int>(s0 + c * kC), hq, h);
-                ++tma_issued;
-            }
             // Shared-memory matrix descriptors, built once: every operand tile's base
             // descriptor plus, per MMA, its byte offset / 16 in the start-address field.
             const uint64_t dK0 = smem_desc_sw128(sbase + OFF_KQ, 16384, 1024);
@@ -286,19 +284,22 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                 ++n_s;
             };
             // Event-driven issue: each MMA batch goes out as soon as its inputs are
-            // ready, state-path batches first.  n8/n10/n6 = next chunk of each batch kind,
+            // ready, state-path batches first.  The loop probes with test_wait, which
+            // never suspends (try_wait may, for a system-defined time, per probe).  n8/n10/n6 = next chunk of each batch kind,
             // nt = next chunk to copy in.
-            int n8 = 0, n10 = 0, n6 = 0, nt = tma_issued;
+            int n8 = 0, n10 = 0, n6 = 0;
             bool ok = true;
             uint64_t t_idle = 0;
+            uint32_t idle = 0;
             while (ok && n10 < nch) {
                 bool progress = false;
-                if (n8 < n6 && mbar_try_wait(b_ss, n8 & 1) && mbar_try_wait(b_w, n8 & 1)) {
+                if (n8 < n6 && mbar_test_wait(b_ss, n8 & 1) && mbar_test_wait(b_w, n8 & 1) &&
+                    (n8 == 0 || mbar_test_wait(b_oread, (n8 - 1) & 1))) {
                     tc_fence_after();
                     mma8(n8++);
                     progress = true;
                 }
-                if (n10 < n8 && mbar_try_wait(b_ds, n10 & 1)) {
+                if (n10 < n8 && mbar_test_wait(b_ds, n10 & 1)) {
                     tc_fence_after();
                     mma10(n10++);
                     progress = true;
@@ -306,32 +307,25 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                 // W^T overwrites the previous chunk's (read by the prep warps before MMA8 of
                 // that chunk went out); U^T reuses the buffer of chunk n6 - 2; and the batch
                 // goes behind the previous chunk's S update, never ahead of it.
-                if (n6 < nch && n6 <= n8 && n6 <= n10 && mbar_try_wait(b_tt, n6 & 1) &&
-                    mbar_try_wait((n6 & 1) ? b_tma1 : b_tma0, (n6 >> 1) & 1)) {
-                    ++tma_waited;
+                if (n6 < nch && n6 <= n8 && n6 <= n10 && mbar_test_wait(b_tt, n6 & 1) &&
+                    mbar_test_wait((n6 & 1) ? b_tma1 : b_tma0, (n6 >> 1) & 1)) {
                     tc_fence_after();
                     mma6(n6++);
                     progress = true;
                 }
-                if (nt < nch && nt - 2 < n10 && mbar_try_wait((nt & 1) ? b_free1 : b_free0, ((nt - 2) >> 1) & 1)) {
-                    const int64_t unit = tc_slot(s0, nt, n) * p.Hv + h;
-                    issue_chunk(&qmap, &kmap, &vmap, sbase, nt & 1, p.ws_P + unit * (kTcPBytes / 2),
-                                p.ws_g + unit * (kTcGateBytes / 4), (nt & 1) ? b_tma1 : b_tma0,
-                                static_cast<int>(s0 + nt * kC), hq, h);
-                    ++tma_issued;
-                    ++nt;
-                    progress = true;
-                }
+                // Idle bookkeeping every 256 empty rounds (the timer read is slow).
                 if (progress) {
-                    t_idle = 0;
-                } else if (t_idle == 0) {
-                    t_idle = global_timer_ns();
-                } else if (*abort) {
-                    ok = false;
-                } else if (global_timer_ns() - t_idle > 2000000000ull) {
-                    atomicExch(&g_tc_error, kWaitIssue);
-                    *abort = 1;
-                    ok = false;
+                    idle = 0;
+                } else if ((++idle & 255u) == 0) {
+                    if (t_idle == 0 || idle == 256) {
+                        t_idle = global_timer_ns();
+                    } else if (*abort) {
+                        ok = false;
+                    } else if (global_timer_ns() - t_idle > 2000000000ull) {
+                        atomicExch(&g_tc_error, kWaitIssue);
+                        *abort = 1;
+                        ok = false;
+                    }
                 }
             }
             if (!ok) {
@@ -340,7 +334,28 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                 if (n_s) wait_bounded(b_s, (n_s - 1) & 1, kWaitS, &never);
                 if (n_d) wait_bounded(b_d, (n_d - 1) & 1, kWaitD, &never);
                 if (n_wu) wait_bounded(b_wu, (n_wu - 1) & 1, kWaitWU, &never);
-                for (int cc = tma_waited; cc < tma_issued; ++cc)
+            }
+        }
+        __syncwarp();
+    } else if (warp == 13) {
+        // ------------------------------------------------------------ copies
+        if (lane == 0) {
+            int issued = 0;
+            bool ok = true;
+            for (int c = 0; c < nch; ++c) {
+                // the last reader of this stage (chunk c - 2's S update) is done
+                if (c >= 2 && !(ok = wait_bounded((c & 1) ? b_free1 : b_free0, ((c - 2) >> 1) & 1, kWaitS, abort)))
+                    break;
+                const int64_t unit = tc_slot(s0, c, n) * p.Hv + h;
+                issue_chunk(&qmap, &kmap, &vmap, sbase, c & 1, p.ws_P + unit * (kTcPBytes / 2),
+                            p.ws_g + unit * (kTcGateBytes / 4), (c & 1) ? b_tma1 : b_tma0,
+                            static_cast<int>(s0 + c * kC), hq, h);
+                ++issued;
+            }
+            if (!ok) {
+                // Give up: wait (bounded) for the copies still in flight.
+                volatile int never = 0;
+                for (int cc = issued > 2 ? issued - 2 : 0; cc < issued; ++cc)
                     wait_bounded((cc & 1) ? b_tma1 : b_tma0, (cc >> 1) & 1, kWaitTma, &never);
             }
         }
@@ -356,6 +371,29 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             bulk_load(sbase + OFF_T, p.ws_T + unit * (kTcTileBytes / 4), kTcTileBytes, b_t);
         };
         if (pt == 0) load_T(0);
+        auto write_out = [&](int c) {
+            uint32_t o[64];
+            tmem_ld32(tmem_addr(tm, lane_base, TM_O), *reinterpret_cast<uint32_t(*)[32]>(o));
+            tmem_ld32(tmem_addr(tm, lane_base, TM_O + 32), *reinterpret_cast<uint32_t(*)[32]>(o + 32));
+            tmem_wait_ld_dep(o);
+            tc_fence_before();
+            warp_arrive(b_oread, lane);
+            const int64_t t0 = s0 + static_cast<int64_t>(c) * kC;
+            const int nt = static_cast<int>(s1 - t0 < kC ? s1 - t0 : kC);
+            __nv_bfloat16 *so = reinterpret_cast<__nv_bfloat16 *>(sm + OFF_O);
+            named_sync(2, 128);   // the previous chunk's rows have left the staging tile
+#pragma unroll
+            for (int ii = 0; ii < 64; ++ii)
+                so[ii * kHeadDim + row] = __float2bfloat16_rn(p.scale * __uint_as_float(o[ii]));
+            named_sync(2, 128);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int idx = pt + 128 * u, i = idx >> 4, c16 = idx & 15;
+                if (i < nt)
+                    *reinterpret_cast<uint4 *>(p.out + ((t0 + i) * p.Hv + h) * kHeadDim + c16 * 8) =
+                        *reinterpret_cast<const uint4 *>(sm + OFF_O + i * 256 + c16 * 16);
+            }
+        };
         for (int c = 0; c < nch; ++c) {
             const int st = c & 1;
             if (!wait_warp(st ? b_tma1 : b_tma0, (c >> 1) & 1, kWaitTma, abort)) break;
@@ -434,14 +472,20 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             fence_proxy_async_smem();
             tc_fence_before();
             warp_arrive(b_w, lane);
+            // the previous chunk's output: O^T (TMEM lane v = column v of O) into registers,
+            // release TM_O, then bf16 staging -> coalesced row stores
+            if (c > 0) {
+                if (!wait_warp(b_s, (c - 1) & 1, kWaitS, abort)) break;
+                write_out(c - 1);
+            }
         }
+        if (nch > 0 && wait_warp(b_s, (nch - 1) & 1, kWaitS, abort)) write_out(nch - 1);
     } else {
         // ------------------------------------------------------------ state path (chunk c)
         // Two halves of four warps (one per TMEM lane quadrant): half hs owns state
         // columns [64 hs, 64 hs + 64) and chunk tokens [32 hs, 32 hs + 32).
         const int v = row;    // state row / token row of this thread's TMEM lane
         const int hs = (warp - 5) >> 2;
-        const int sg = tid - 160 - 128 * hs;
         {
             const float *src = p.state ? p.state + (chain * kHeadDim + v) * kHeadDim : nullptr;
 #pragma unroll 1
@@ -458,36 +502,11 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                 tmem_wait_st();
             }
         }
-        // This half's 32 token columns of O^T (TMEM lane v = column v of O) -> bf16 staging
-        // -> coalesced row stores.
-        auto write_out = [&](const uint32_t (&o)[32], int c) {
-            const int64_t t0 = s0 + static_cast<int64_t>(c) * kC;
-            const int nt = static_cast<int>(s1 - t0 < kC ? s1 - t0 : kC);
-            uint8_t *stage = sm + OFF_O + hs * 8192;
-            __nv_bfloat16 *so = reinterpret_cast<__nv_bfloat16 *>(stage);
-            named_sync(3 + hs, 128);
-#pragma unroll
-            for (int ii = 0; ii < 32; ++ii)
-                so[ii * kHeadDim + v] = __float2bfloat16_rn(p.scale * __uint_as_float(o[ii]));
-            named_sync(3 + hs, 128);
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int idx = sg + 128 * u, r32 = idx >> 4, c16 = idx & 15, i = 32 * hs + r32;
-                if (i < nt)
-                    *reinterpret_cast<uint4 *>(p.out + ((t0 + i) * p.Hv + h) * kHeadDim + c16 * 8) =
-                        *reinterpret_cast<const uint4 *>(stage + r32 * 256 + c16 * 16);
-            }
-        };
         bool ok = true;
-        uint32_t o[32];
         for (int c = 0; c < nch; ++c) {
             const int st = c & 1;
-            if (c > 0) {
-                // the previous chunk's S update and output are done: take its O^T columns
-                if (!(ok = wait_warp(b_s, (c - 1) & 1, kWaitS, abort))) break;
-                tmem_ld32(tmem_addr(tm, lane_base, TM_O + 32 * hs), o);
-                tmem_wait_ld_dep(o);
-            }
+            // the previous chunk's S update is done
+            if (c > 0 && !(ok = wait_warp(b_s, (c - 1) & 1, kWaitS, abort))) break;
             if (!(ok = wait_warp(st ? b_tma1 : b_tma0, (c >> 1) & 1, kWaitTma, abort))) break;
             const float *g_beta = reinterpret_cast<const float *>(sm + OFF_GST + st * kTcGateBytes);
             const float *g_Gam = g_beta + 128, *g_dec = g_beta + 192;
@@ -542,13 +561,8 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             }
             tc_fence_before();
             warp_arrive(b_ds, lane);
-            // the previous chunk's output goes out while this chunk's S update runs
-            if (c > 0) write_out(o, c - 1);
         }
         if (ok && wait_warp(b_s, (nch - 1) & 1, kWaitS, abort)) {
-            tmem_ld32(tmem_addr(tm, lane_base, TM_O + 32 * hs), o);
-            tmem_wait_ld_dep(o);
-            write_out(o, nch - 1);
             float *dst = dst_state + v * kHeadDim;
 #pragma unroll 1
             for (int q4 = 2 * hs; q4 < 2 * hs + 2; ++q4) {

@@ -1,6 +1,6 @@
 """Small, self-contained launches of each kernel for profiling under ncu.
 
-    python -m fastaf_kernel_b200.profile_cases prefill --seq-len 4096 [--method chunked]
+    python -m fastaf_kernel_b200.profile_cases prefill --seq-len 4096 [--method tcgen05]
     python -m fastaf_kernel_b200.profile_cases decode --batch 512
 
 Each case builds its seeded inputs on cuda:0, runs the kernel a few times (so a
@@ -45,7 +45,7 @@ def main(argv=None) -> int:
     p = sub.add_parser("prefill")
     p.add_argument("--seq-len", type=int, default=4096)
     p.add_argument("--n-seqs", type=int, default=16)
-    p.add_argument("--method", choices=["auto", "chunked", "recurrent"], default="chunked")
+    p.add_argument("--method", choices=["auto", "tcgen05", "chunked", "recurrent"], default="tcgen05")
     p.add_argument("--launches", type=int, default=2)
     d = sub.add_parser("decode")
     d.add_argument("--batch", type=int, default=512)
