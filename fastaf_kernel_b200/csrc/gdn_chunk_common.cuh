@@ -14,6 +14,15 @@ __device__ __forceinline__ void split_bf16(float x, float &hi, float &lo) {
     lo = x - hi;
 }
 
+// The same split for two values at once, packed (a in bits 0-15): hi = bf16(a, b)
+// rounded to nearest even, lo = bf16 of the exact fp32 remainders.
+__device__ __forceinline__ void split2_bf16(float a, float b, uint32_t &hi, uint32_t &lo) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    hi = *reinterpret_cast<uint32_t *>(&h);
+    __nv_bfloat162 l = __floats2bfloat162_rn(a - __uint_as_float(hi << 16), b - __uint_as_float(hi & 0xffff0000u));
+    lo = *reinterpret_cast<uint32_t *>(&l);
+}
+
 // Byte offset of element (row, col) of a bf16 tile whose rows are `kRowBytes`
 // long (128 or 256), with the 16-byte chunk index XOR-ed by (row & 7): eight
 // consecutive rows at the same logical chunk land in eight different banks, so

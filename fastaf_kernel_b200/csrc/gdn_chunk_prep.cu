@@ -1,7 +1,8 @@
 // gdn_chunk_prep.cu -- the state-independent half of the chunked prefill, for every
-// chunk of every sequence at once: the chunk's gates, T = (I + A)^-1 and the decayed
-// Q K^T tile P, written to the workspace of gdn_tc_workspace.h that the tcgen05 chain
-// kernel (gdn_prefill_tc.cu) streams in.
+// chunk of every sequence at once: the chunk's gates, T = (I + A)^-1 scaled into the
+// bf16 hi/lo operand tiles T' = T diag(beta) and T'' = T diag(beta Gamma), and the
+// decayed Q K^T tile P, written to the workspace of gdn_tc_workspace.h that the
+// tcgen05 chain kernel (gdn_prefill_tc.cu) streams in.
 //
 // For a chunk of tokens i, j = 0..63 (solution/gdn_baseline_torch.py:42-44, 71-87):
 //   log alpha_i = -exp(A_log) softplus(a_i + dt_bias),  beta_i = sigmoid(b_i)
@@ -60,7 +61,8 @@ struct PrepParams {
     int64_t T;
     int Hq, Hv, groups;
     int gate_dtype, param_dtype;
-    float *ws_T, *ws_g;
+    uint8_t *ws_T;
+    float *ws_g;
     __nv_bfloat16 *ws_P;
 };
 
@@ -362,19 +364,30 @@ __global__ void __launch_bounds__(kThreads, 4) chunk_prep_kernel(const PrepParam
         }
         __syncthreads();
 
-        // T (row-major, zero above the diagonal) and the gate vectors to the workspace.
-        float *dT = p.ws_T + unit * (kTcTileBytes / 4);
+        // T' = T diag(beta) and T'' = T diag(beta Gamma) (zero above the diagonal) as bf16
+        // hi/lo tiles, and the gate vectors, to the workspace.  Thread (i, ch) writes the
+        // 16-byte chunk ch of row i of each tile.
+        uint8_t *dT = p.ws_T + unit * kTcTBytes;
 #pragma unroll
-        for (int u = 0; u < (64 * 16) / kThreads; ++u) {
-            const int idx = tid + u * kThreads;
-            const int i = idx >> 4, j = (idx & 15) * 4;
-            const float4 t = *reinterpret_cast<const float4 *>(T_f + i * 64 + j);
-            float4 val;
-            val.x = j <= i ? t.x : 0.0f;
-            val.y = j + 1 <= i ? t.y : 0.0f;
-            val.z = j + 2 <= i ? t.z : 0.0f;
-            val.w = j + 3 <= i ? t.w : 0.0f;
-            *reinterpret_cast<float4 *>(dT + i * 64 + j) = val;
+        for (int u = 0; u < (64 * 8) / kThreads; ++u) {
+            const int idx = tid + u * kThreads, i = idx >> 3, ch = idx & 7;
+            const float4 ta = *reinterpret_cast<const float4 *>(T_f + i * 64 + ch * 8);
+            const float4 tb = *reinterpret_cast<const float4 *>(T_f + i * 64 + ch * 8 + 4);
+            const float t[8] = {ta.x, ta.y, ta.z, ta.w, tb.x, tb.y, tb.z, tb.w};
+            uint32_t w1h[4], w1l[4], w2h[4], w2l[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int j = ch * 8 + 2 * e;
+                const float a0 = (j <= i ? t[2 * e] : 0.0f) * g_beta[j];
+                const float a1 = (j + 1 <= i ? t[2 * e + 1] : 0.0f) * g_beta[j + 1];
+                split2_bf16(a0, a1, w1h[e], w1l[e]);
+                split2_bf16(a0 * g_Gam[j], a1 * g_Gam[j + 1], w2h[e], w2l[e]);
+            }
+            uint8_t *d = dT + swz<128>(i, ch * 8);
+            *reinterpret_cast<uint4 *>(d) = make_uint4(w1h[0], w1h[1], w1h[2], w1h[3]);
+            *reinterpret_cast<uint4 *>(d + kTcTileBytes) = make_uint4(w1l[0], w1l[1], w1l[2], w1l[3]);
+            *reinterpret_cast<uint4 *>(d + 2 * kTcTileBytes) = make_uint4(w2h[0], w2h[1], w2h[2], w2h[3]);
+            *reinterpret_cast<uint4 *>(d + 3 * kTcTileBytes) = make_uint4(w2l[0], w2l[1], w2l[2], w2l[3]);
         }
         p.ws_g[unit * (kTcGateBytes / 4) + tid] = g_beta[tid];
         p.ws_g[unit * (kTcGateBytes / 4) + 128 + tid] = g_beta[128 + tid];
@@ -391,7 +404,7 @@ int prep_groups(int64_t chains) {
     return static_cast<int>(gsz < 1 ? 1 : (gsz > 64 ? 64 : gsz));
 }
 
-cudaError_t launch_chunk_prep(const PrefillArgs &p, float *ws_T, __nv_bfloat16 *ws_P, float *ws_g,
+cudaError_t launch_chunk_prep(const PrefillArgs &p, uint8_t *ws_T, __nv_bfloat16 *ws_P, float *ws_g,
                               cudaStream_t stream) {
     const int64_t chains = p.num_seqs * p.Hv;
     if (chains == 0) return cudaSuccess;

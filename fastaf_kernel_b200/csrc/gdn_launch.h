@@ -45,7 +45,7 @@ bool prefill_chunked_supported(const PrefillArgs &p);
 cudaError_t launch_prefill_tc(const PrefillArgs &p, void *workspace, cudaStream_t stream);
 bool prefill_tc_supported(const PrefillArgs &p);
 size_t prefill_tc_workspace_bytes(const PrefillArgs &p);
-cudaError_t launch_chunk_prep(const PrefillArgs &p, float *ws_T, __nv_bfloat16 *ws_P, float *ws_g,
+cudaError_t launch_chunk_prep(const PrefillArgs &p, uint8_t *ws_T, __nv_bfloat16 *ws_P, float *ws_g,
                               cudaStream_t stream);
 // Site of the first bounded device wait of the tcgen05 prefill that gave up (0 = none).
 cudaError_t read_tc_device_error(cudaStream_t stream, int *code, bool clear);

@@ -13,7 +13,7 @@
 // gdn_prefill_ws from the caller; this entry point needs neither.
 //
 // The array holds kNoAllocWorkspaceBytes (64 MiB), enough for
-// (ceil(T/64) + N) * Hv <= 2621 chunk-head slots, e.g. T = 4608 tokens in up to 8
+// (ceil(T/64) + N) * Hv <= 1598 chunk-head slots, e.g. T = 2560 tokens in up to 9
 // sequences with 32 v-heads.  Larger calls are rejected before any launch.  Nothing in
 // the array has to start at zero: the prep kernel writes every slot the chain kernel
 // reads, in the same call.  There is one array per device, so calls whose executions

@@ -12,8 +12,9 @@
 //   O     = scale (diag(Gamma) Q S0^T + P delta),  P[i][j] = exp(gamma_i - gamma_j) q_i.k_j (j <= i)
 //   S_end = Gamma_63 S0 + sum_i exp(gamma_63 - gamma_i) delta_i k_i^T
 //
-// The state-independent inputs of every chunk -- its gates, T and P -- come from
-// gdn_chunk_prep.cu through a workspace (gdn_tc_workspace.h).  Padding tokens of a
+// The state-independent inputs of every chunk -- its gates, the T' = T diag(beta) and
+// T'' = T diag(beta Gamma) operand tiles and P -- come from gdn_chunk_prep.cu through
+// a workspace (gdn_tc_workspace.h).  Padding tokens of a
 // partial chunk have beta = 0 and log alpha = 0.  Every product with an fp32 operand
 // (S0, T, W, the decayed delta) splits it into bf16 hi + lo.
 //
@@ -21,12 +22,13 @@
 // each other through mbarriers, so the next chunk's state-independent products run
 // while the current chunk's state update is on the tensor core:
 //   warp 0      allocates all 512 TMEM columns; lane 0 issues every MMA, each batch as
-//               soon as its inputs are ready, state path first
-//   warp 13     lane 0 issues the copies of each chunk (TMA tiles, bulk P and gates) as
-//               soon as the chunk two back has left its stage
-//   warps 1-4   prep (one per TMEM lane quadrant): T' = T diag(beta), T'' = T diag(beta
-//               Gamma) and diag(Gamma) Q tiles, -W from W^T in TMEM, then the previous
-//               chunk's output rows from O^T in TMEM
+//               soon as its inputs are ready, state path first: per chunk c the order
+//               on the tensor pipe is  W^T(c), [S update(c-1)], U^T(c), delta(c), ...
+//               so W^T is computed while the previous innovation is being split
+//   warp 13     lane 0 issues the copies of each chunk (TMA tiles, bulk T tiles, P and
+//               gates) as soon as their previous readers are done
+//   warps 1-4   prep (one per TMEM lane quadrant): the diag(Gamma) Q tile, -W from W^T
+//               in TMEM, then the previous chunk's output rows from O^T in TMEM
 //   warps 5-12  state path, two halves of four warps: S -> hi/lo split and decay, the
 //               innovation split
 // The fp32 state lives in TMEM columns [0,128) for the whole sequence.
@@ -61,18 +63,19 @@ constexpr uint32_t OFF_KQ = 0;              // 2 stages x 32 KB: [K_h0 | Q_h0 | 
 constexpr uint32_t KQ_STAGE = 32 * 1024;
 constexpr uint32_t OFF_V = 64 * 1024;       // 2 stages x 16 KB: [V_h0 | V_h1]
 constexpr uint32_t V_STAGE = 16 * 1024;
-constexpr uint32_t OFF_T = 96 * 1024;       // 16 KB: fp32 T [64][64] of the chunk the prep warps work on
-constexpr uint32_t OFF_QS = 112 * 1024;     // 16 KB: diag(Gamma) Q, K-major [i][k]
-constexpr uint32_t OFF_P = 128 * 1024;      // 2 stages x 8 KB: P, K-major [i][j] (from the workspace)
-constexpr uint32_t OFF_T1H = 144 * 1024;    // 8 KB each: T diag(beta) hi/lo, T diag(beta Gamma) hi/lo
-constexpr uint32_t OFF_T1L = 152 * 1024;
-constexpr uint32_t OFF_T2H = 160 * 1024;
-constexpr uint32_t OFF_T2L = 168 * 1024;
-constexpr uint32_t OFF_WH = 176 * 1024;     // 16 KB each: -W hi/lo, MN-major [k][i]
-constexpr uint32_t OFF_WL = 192 * 1024;
-constexpr uint32_t OFF_O = 208 * 1024;      // 16 KB: bf16 [64][128] output staging
-constexpr uint32_t OFF_GST = 224 * 1024;    // 2 stages x 1 KB: beta, gamma*log2(e), Gamma, decay-to-end
-constexpr uint32_t SMEM_BYTES = 226 * 1024;
+constexpr uint32_t OFF_O = 96 * 1024;       // 16 KB: bf16 [64][128] output staging
+constexpr uint32_t OFF_P = 112 * 1024;      // 2 stages x 8 KB: P, K-major [i][j] (from the workspace)
+constexpr uint32_t OFF_T1H = 128 * 1024;    // 8 KB each, K-major [i][j] (from the workspace):
+constexpr uint32_t OFF_T1L = 136 * 1024;    //   T' = T diag(beta) hi/lo, T'' = T diag(beta Gamma) hi/lo
+constexpr uint32_t OFF_T2H = 144 * 1024;
+constexpr uint32_t OFF_T2L = 152 * 1024;
+constexpr uint32_t OFF_WH = 160 * 1024;     // 16 KB each: -W hi/lo, MN-major [k][i]
+constexpr uint32_t OFF_WL = 176 * 1024;
+constexpr uint32_t OFF_QS = 192 * 1024;     // 16 KB: diag(Gamma) Q, K-major [i][k]
+constexpr uint32_t OFF_GST = 208 * 1024;    // 2 stages x 1 KB: beta, gamma*log2(e), Gamma, decay-to-end
+constexpr uint32_t SMEM_BYTES = 210 * 1024;
+static_assert(OFF_T1L - OFF_T1H == kTcTileBytes && OFF_T2H - OFF_T1H == 2 * kTcTileBytes,
+              "T tiles sit in shared memory in their workspace order");
 constexpr uint32_t kStageTx = 6 * 8192 + kTcPBytes + kTcGateBytes;
 
 // TMEM columns (all 512 allocated).
@@ -87,7 +90,7 @@ constexpr uint32_t TM_W = 384;    // [384,448) W^T (lanes k, columns i)
 constexpr uint32_t TM_O = 448;    // [448,512) (Gamma Q S^T)^T, then O^T
 
 enum WaitSite { kWaitTma = 1, kWaitWU = 3, kWaitD = 4, kWaitS = 5, kWaitTT = 6,
-                kWaitW = 7, kWaitSS = 8, kWaitDS = 9, kWaitT = 10, kWaitIssue = 11 };
+                kWaitW = 7, kWaitSS = 8, kWaitDS = 9, kWaitT = 10, kWaitIssue = 11, kWaitUD = 12 };
 // (output reads O^T of chunk c before the delta batch of chunk c + 1 overwrites it)
 
 struct TcParams {
@@ -98,12 +101,13 @@ struct TcParams {
     float scale;
     __nv_bfloat16 *out;
     float *new_state;
-    const float *ws_T, *ws_g;
+    const uint8_t *ws_T;
+    const float *ws_g;
     const __nv_bfloat16 *ws_P;
 };
 
 struct Bars {
-    uint64_t tma[2], wu, d, s, tt, w, ss, ds, t, free_[2], oread;
+    uint64_t tma[2], wdone, udone, d, s, qs, w, ss, ds, tw, tu, free_[2], oread;
 };
 
 __device__ __forceinline__ void issue_chunk(const CUtensorMap *qmap, const CUtensorMap *kmap,
@@ -177,9 +181,11 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
     const int nch = static_cast<int>((s1 - s0 + kC - 1) / kC);
     const uint32_t sbase = smem_u32(sm);
     const uint32_t b_tma0 = smem_u32(&bars.tma[0]), b_tma1 = smem_u32(&bars.tma[1]);
-    const uint32_t b_wu = smem_u32(&bars.wu), b_d = smem_u32(&bars.d);
-    const uint32_t b_s = smem_u32(&bars.s), b_tt = smem_u32(&bars.tt), b_w = smem_u32(&bars.w);
-    const uint32_t b_ss = smem_u32(&bars.ss), b_ds = smem_u32(&bars.ds), b_t = smem_u32(&bars.t);
+    // wdone / udone: the W^T / U^T batch of a chunk is done; tw / tu: its T'' / T' tiles arrived
+    const uint32_t b_wdone = smem_u32(&bars.wdone), b_udone = smem_u32(&bars.udone), b_d = smem_u32(&bars.d);
+    const uint32_t b_s = smem_u32(&bars.s), b_qs = smem_u32(&bars.qs), b_w = smem_u32(&bars.w);
+    const uint32_t b_ss = smem_u32(&bars.ss), b_ds = smem_u32(&bars.ds);
+    const uint32_t b_tw = smem_u32(&bars.tw), b_tu = smem_u32(&bars.tu);
     // free[b]: chunk c's S-update batch (the last reader of stage c & 1 and P buffer c & 1) is done
     const uint32_t b_free0 = smem_u32(&bars.free_[0]), b_free1 = smem_u32(&bars.free_[1]);
     const uint32_t b_oread = smem_u32(&bars.oread);   // the prep warps have read O^T of a chunk
@@ -189,14 +195,16 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         if (lane == 0) {
             mbar_init(b_tma0, 1);
             mbar_init(b_tma1, 1);
-            mbar_init(b_wu, 1);
+            mbar_init(b_wdone, 1);
+            mbar_init(b_udone, 1);
             mbar_init(b_d, 1);
             mbar_init(b_s, 1);
-            mbar_init(b_tt, 4);
+            mbar_init(b_qs, 4);
             mbar_init(b_w, 4);
             mbar_init(b_ss, 8);
             mbar_init(b_ds, 8);
-            mbar_init(b_t, 1);
+            mbar_init(b_tw, 1);
+            mbar_init(b_tu, 1);
             mbar_init(b_free0, 1);
             mbar_init(b_free1, 1);
             mbar_init(b_oread, 4);
@@ -219,7 +227,6 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
     } else if (warp == 0) {
         // ------------------------------------------------------------ MMA issue
         if (lane == 0) {
-            int n_wu = 0, n_d = 0, n_s = 0;
             // Shared-memory matrix descriptors, built once: every operand tile's base
             // descriptor plus, per MMA, its byte offset / 16 in the start-address field.
             const uint64_t dK0 = smem_desc_sw128(sbase + OFF_KQ, 16384, 1024);
@@ -232,22 +239,24 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             // (the lo tiles sit 8 or 16 KB above the hi tiles; stage 1 one stage above stage 0)
             constexpr uint64_t kLoT = (OFF_T1L - OFF_T1H) >> 4, kLoW = (OFF_WL - OFF_WH) >> 4;
             static_assert(OFF_T2L - OFF_T2H == OFF_T1L - OFF_T1H, "T' / T'' hi-lo spacing");
-            auto mma6 = [&](int c) {    // W^T -> TM_W, U^T -> TM_U[c & 1]
-                const int st = c & 1;
-                const uint32_t tu = TM_U0 + st * 64;
-                constexpr uint32_t id = idesc_bf16_f32(128, 64, true, false);
+            constexpr uint32_t id6 = idesc_bf16_f32(128, 64, true, false);
+            auto mma6w = [&](int c) {   // W^T = K^T T''^T -> TM_W
 #pragma unroll
-                for (int part = 0; part < 2; ++part) {
+                for (int part = 0; part < 2; ++part)
 #pragma unroll
-                    for (int s = 0; s < 4; ++s) {
-                        mma_ss(tm + TM_W, dK0 + st * (KQ_STAGE >> 4) + 128 * s, dT2h + part * kLoT + 2 * s, id,
-                               part | s);
-                        mma_ss(tm + tu, dV0 + st * (V_STAGE >> 4) + 128 * s, dT1h + part * kLoT + 2 * s, id,
-                               part | s);
-                    }
-                }
-                mma_commit(b_wu);
-                ++n_wu;
+                    for (int s = 0; s < 4; ++s)
+                        mma_ss(tm + TM_W, dK0 + (c & 1) * (KQ_STAGE >> 4) + 128 * s, dT2h + part * kLoT + 2 * s,
+                               id6, part | s);
+                mma_commit(b_wdone);
+            };
+            auto mma6u = [&](int c) {   // U^T = V^T T'^T -> TM_U[c & 1]
+#pragma unroll
+                for (int part = 0; part < 2; ++part)
+#pragma unroll
+                    for (int s = 0; s < 4; ++s)
+                        mma_ss(tm + TM_U0 + (c & 1) * 64, dV0 + (c & 1) * (V_STAGE >> 4) + 128 * s,
+                               dT1h + part * kLoT + 2 * s, id6, part | s);
+                mma_commit(b_udone);
             };
             auto mma8 = [&](int c) {    // delta^T = U^T - S W^T -> TM_U[c & 1]; (Gamma Q S^T)^T -> TM_O
                 const uint32_t tu = TM_U0 + (c & 1) * 64;
@@ -264,7 +273,6 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                 for (int s = 0; s < 8; ++s)
                     mma_ts(tm + TM_O, tm + TM_SHI + 8 * s, dQS + (s >> 2) * 512 + (s & 3) * 2, idq, s > 0);
                 mma_commit(b_d);
-                ++n_d;
             };
             auto mma10 = [&](int c) {   // S += delta'^T K, O^T += delta^T P^T
                 const int st = c & 1;
@@ -281,36 +289,42 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                     mma_ts(tm + TM_O, tm + TM_DBF + 8 * s, dP0 + st * (kTcPBytes >> 4) + 2 * s, ido, 1);
                 mma_commit(b_s);
                 mma_commit(st ? b_free1 : b_free0);
-                ++n_s;
             };
             // Event-driven issue: each MMA batch goes out as soon as its inputs are
             // ready, state-path batches first.  The loop probes with test_wait, which
-            // never suspends (try_wait may, for a system-defined time, per probe).  n8/n10/n6 = next chunk of each batch kind,
-            // nt = next chunk to copy in.
-            int n8 = 0, n10 = 0, n6 = 0;
+            // never suspends (try_wait may, for a system-defined time, per probe).
+            // n6w / n6u / n8 / n10 = next chunk of each batch kind.
+            int n6w = 0, n6u = 0, n8 = 0, n10 = 0;
             bool ok = true;
             uint64_t t_idle = 0;
             uint32_t idle = 0;
             while (ok && n10 < nch) {
                 bool progress = false;
-                if (n8 < n6 && mbar_test_wait(b_ss, n8 & 1) && mbar_test_wait(b_w, n8 & 1) &&
-                    (n8 == 0 || mbar_test_wait(b_oread, (n8 - 1) & 1))) {
-                    tc_fence_after();
-                    mma8(n8++);
-                    progress = true;
-                }
                 if (n10 < n8 && mbar_test_wait(b_ds, n10 & 1)) {
                     tc_fence_after();
                     mma10(n10++);
                     progress = true;
                 }
-                // W^T overwrites the previous chunk's (read by the prep warps before MMA8 of
-                // that chunk went out); U^T reuses the buffer of chunk n6 - 2; and the batch
-                // goes behind the previous chunk's S update, never ahead of it.
-                if (n6 < nch && n6 <= n8 && n6 <= n10 && mbar_test_wait(b_tt, n6 & 1) &&
-                    mbar_test_wait((n6 & 1) ? b_tma1 : b_tma0, (n6 >> 1) & 1)) {
+                // delta goes behind its U^T batch; TM_O must have been read out
+                if (n8 < n6u && mbar_test_wait(b_ss, n8 & 1) && mbar_test_wait(b_w, n8 & 1) &&
+                    mbar_test_wait(b_qs, n8 & 1) && (n8 == 0 || mbar_test_wait(b_oread, (n8 - 1) & 1))) {
                     tc_fence_after();
-                    mma6(n6++);
+                    mma8(n8++);
+                    progress = true;
+                }
+                // W^T overwrites the previous chunk's, which the prep warps turned into -W
+                // before the previous delta batch went out
+                if (n6w < nch && n6w <= n8 && mbar_test_wait(b_tw, n6w & 1) &&
+                    mbar_test_wait((n6w & 1) ? b_tma1 : b_tma0, (n6w >> 1) & 1)) {
+                    tc_fence_after();
+                    mma6w(n6w++);
+                    progress = true;
+                }
+                // U^T reuses the buffer of chunk n6u - 2 and goes behind the previous
+                // chunk's S update, never ahead of it
+                if (n6u < n6w && n6u <= n10 && mbar_test_wait(b_tu, n6u & 1)) {
+                    tc_fence_after();
+                    mma6u(n6u++);
                     progress = true;
                 }
                 // Idle bookkeeping every 256 empty rounds (the timer read is slow).
@@ -328,49 +342,56 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                     }
                 }
             }
-            if (!ok) {
-                // Give up: wait (bounded) for every MMA and copy still in flight.
-                volatile int never = 0;
-                if (n_s) wait_bounded(b_s, (n_s - 1) & 1, kWaitS, &never);
-                if (n_d) wait_bounded(b_d, (n_d - 1) & 1, kWaitD, &never);
-                if (n_wu) wait_bounded(b_wu, (n_wu - 1) & 1, kWaitWU, &never);
-            }
+            // Wait (bounded, also after a give-up) for the last commit of every kind, so
+            // no MMA or barrier arrive is still in flight when the CTA leaves.
+            volatile int never = 0;
+            if (n6w) wait_bounded(b_wdone, (n6w - 1) & 1, kWaitWU, &never);
+            if (n6u) wait_bounded(b_udone, (n6u - 1) & 1, kWaitUD, &never);
+            if (n8) wait_bounded(b_d, (n8 - 1) & 1, kWaitD, &never);
+            if (n10) wait_bounded(b_s, (n10 - 1) & 1, kWaitS, &never);
+            for (int c = n10 > 2 ? n10 - 2 : 0; c < n10; ++c)
+                wait_bounded((c & 1) ? b_free1 : b_free0, (c >> 1) & 1, kWaitS, &never);
         }
         __syncwarp();
     } else if (warp == 13) {
         // ------------------------------------------------------------ copies
+        // Per chunk c, in the order the previous readers finish: the T'' tiles once the
+        // W^T batch of c - 1 is done, the stage (K, Q, V, P, gates) once the S update of
+        // c - 2 is done, the T' tiles once the U^T batch of c - 1 is done.
         if (lane == 0) {
-            int issued = 0;
+            int issued = 0, n_tw = 0, n_tu = 0;
             bool ok = true;
+            auto unit_of = [&](int c) { return tc_slot(s0, c, n) * p.Hv + h; };
             for (int c = 0; c < nch; ++c) {
-                // the last reader of this stage (chunk c - 2's S update) is done
+                const int64_t unit = unit_of(c);
+                if (c >= 1 && !(ok = wait_bounded(b_wdone, (c - 1) & 1, kWaitWU, abort))) break;
+                mbar_arrive_expect_tx(b_tw, 2 * kTcTileBytes);
+                bulk_load(sbase + OFF_T2H, p.ws_T + unit * kTcTBytes + 2 * kTcTileBytes, 2 * kTcTileBytes, b_tw);
+                ++n_tw;
                 if (c >= 2 && !(ok = wait_bounded((c & 1) ? b_free1 : b_free0, ((c - 2) >> 1) & 1, kWaitS, abort)))
                     break;
-                const int64_t unit = tc_slot(s0, c, n) * p.Hv + h;
                 issue_chunk(&qmap, &kmap, &vmap, sbase, c & 1, p.ws_P + unit * (kTcPBytes / 2),
                             p.ws_g + unit * (kTcGateBytes / 4), (c & 1) ? b_tma1 : b_tma0,
                             static_cast<int>(s0 + c * kC), hq, h);
                 ++issued;
+                if (c >= 1 && !(ok = wait_bounded(b_udone, (c - 1) & 1, kWaitUD, abort))) break;
+                mbar_arrive_expect_tx(b_tu, 2 * kTcTileBytes);
+                bulk_load(sbase + OFF_T1H, p.ws_T + unit * kTcTBytes, 2 * kTcTileBytes, b_tu);
+                ++n_tu;
             }
             if (!ok) {
                 // Give up: wait (bounded) for the copies still in flight.
                 volatile int never = 0;
                 for (int cc = issued > 2 ? issued - 2 : 0; cc < issued; ++cc)
                     wait_bounded((cc & 1) ? b_tma1 : b_tma0, (cc >> 1) & 1, kWaitTma, &never);
+                if (n_tw) wait_bounded(b_tw, (n_tw - 1) & 1, kWaitT, &never);
+                if (n_tu) wait_bounded(b_tu, (n_tu - 1) & 1, kWaitT, &never);
             }
         }
         __syncwarp();
     } else if (warp <= 4) {
         // ------------------------------------------------------------ prep (chunk c + 1 while c runs)
         const int pt = tid - 32;    // 0..127
-        // T of the chunk this group works on: one buffer, refilled by thread pt == 0 once
-        // every prep thread has converted the previous chunk's T.
-        auto load_T = [&](int c) {
-            const int64_t unit = tc_slot(s0, c, n) * p.Hv + h;
-            mbar_arrive_expect_tx(b_t, kTcTileBytes);
-            bulk_load(sbase + OFF_T, p.ws_T + unit * (kTcTileBytes / 4), kTcTileBytes, b_t);
-        };
-        if (pt == 0) load_T(0);
         auto write_out = [&](int c) {
             uint32_t o[64];
             tmem_ld32(tmem_addr(tm, lane_base, TM_O), *reinterpret_cast<uint32_t(*)[32]>(o));
@@ -397,35 +418,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         for (int c = 0; c < nch; ++c) {
             const int st = c & 1;
             if (!wait_warp(st ? b_tma1 : b_tma0, (c >> 1) & 1, kWaitTma, abort)) break;
-            if (!wait_warp(b_t, c & 1, kWaitT, abort)) break;
-            const float *g_beta = reinterpret_cast<const float *>(sm + OFF_GST + st * kTcGateBytes);
-            const float *g_Gam = g_beta + 128;
-            const float *T_s = reinterpret_cast<const float *>(sm + OFF_T);
-            // T' = T diag(beta), T'' = T diag(beta Gamma) as bf16 hi/lo (K-major [i][j])
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int idx = pt + 128 * u, i = idx >> 3, ch = idx & 7;
-                uint32_t w1h[4], w1l[4], w2h[4], w2l[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int j = ch * 8 + 2 * e;
-                    const float2 t = *reinterpret_cast<const float2 *>(T_s + i * 64 + j);
-                    const float a0 = t.x * g_beta[j], a1 = t.y * g_beta[j + 1];
-                    const float b0 = a0 * g_Gam[j], b1 = a1 * g_Gam[j + 1];
-                    float h0, l0, h1, l1;
-                    split_bf16(a0, h0, l0); split_bf16(a1, h1, l1);
-                    w1h[e] = pack_bf16x2(h0, h1); w1l[e] = pack_bf16x2(l0, l1);
-                    split_bf16(b0, h0, l0); split_bf16(b1, h1, l1);
-                    w2h[e] = pack_bf16x2(h0, h1); w2l[e] = pack_bf16x2(l0, l1);
-                }
-                const uint32_t off = sw128(i, ch);
-                *reinterpret_cast<uint4 *>(sm + OFF_T1H + off) = make_uint4(w1h[0], w1h[1], w1h[2], w1h[3]);
-                *reinterpret_cast<uint4 *>(sm + OFF_T1L + off) = make_uint4(w1l[0], w1l[1], w1l[2], w1l[3]);
-                *reinterpret_cast<uint4 *>(sm + OFF_T2H + off) = make_uint4(w2h[0], w2h[1], w2h[2], w2h[3]);
-                *reinterpret_cast<uint4 *>(sm + OFF_T2L + off) = make_uint4(w2l[0], w2l[1], w2l[2], w2l[3]);
-            }
-            named_sync(2, 128);   // every prep thread has read T: refill it with the next chunk's
-            if (pt == 0 && c + 1 < nch) load_T(c + 1);
+            const float *g_Gam = reinterpret_cast<const float *>(sm + OFF_GST + st * kTcGateBytes) + 128;
             // diag(Gamma) Q once the previous chunk's Q S^T product has read the tile
             if (c > 0 && !wait_warp(b_d, (c - 1) & 1, kWaitD, abort)) break;
             {
@@ -445,9 +438,9 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             }
             fence_proxy_async_smem();
             tc_fence_before();
-            warp_arrive(b_tt, lane);
+            warp_arrive(b_qs, lane);
             // -W as bf16 hi/lo, MN-major [k][i] (TMEM lane k holds row k of W^T)
-            if (!wait_warp(b_wu, c & 1, kWaitWU, abort)) break;
+            if (!wait_warp(b_wdone, c & 1, kWaitWU, abort)) break;
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
                 uint32_t r[32];
@@ -457,13 +450,9 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                 for (int cq = 0; cq < 4; ++cq) {
                     uint32_t wh[4], wl[4];
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        float h0, l0, h1, l1;
-                        split_bf16(-__uint_as_float(r[cq * 8 + 2 * e]), h0, l0);
-                        split_bf16(-__uint_as_float(r[cq * 8 + 2 * e + 1]), h1, l1);
-                        wh[e] = pack_bf16x2(h0, h1);
-                        wl[e] = pack_bf16x2(l0, l1);
-                    }
+                    for (int e = 0; e < 4; ++e)
+                        split2_bf16(-__uint_as_float(r[cq * 8 + 2 * e]), -__uint_as_float(r[cq * 8 + 2 * e + 1]),
+                                    wh[e], wl[e]);
                     const uint32_t off = sw128(row, 4 * hf + cq);
                     *reinterpret_cast<uint4 *>(sm + OFF_WH + off) = make_uint4(wh[0], wh[1], wh[2], wh[3]);
                     *reinterpret_cast<uint4 *>(sm + OFF_WL + off) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
@@ -519,13 +508,8 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                     tmem_ld32(tmem_addr(tm, lane_base, TM_S + 32 * q4), r);
                     tmem_wait_ld_dep(r);
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        float h0, l0, h1, l1;
-                        split_bf16(__uint_as_float(r[2 * j]), h0, l0);
-                        split_bf16(__uint_as_float(r[2 * j + 1]), h1, l1);
-                        hi[j] = pack_bf16x2(h0, h1);
-                        lo[j] = pack_bf16x2(l0, l1);
-                    }
+                    for (int j = 0; j < 16; ++j)
+                        split2_bf16(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]), hi[j], lo[j]);
                     tmem_st16(tmem_addr(tm, lane_base, TM_SHI + 16 * q4), hi);
                     tmem_st16(tmem_addr(tm, lane_base, TM_SLO + 16 * q4), lo);
 #pragma unroll
@@ -548,11 +532,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                     const int i0 = hs * 32 + 2 * e, i1 = i0 + 1;
                     const float d0 = __uint_as_float(r[2 * e]), d1 = __uint_as_float(r[2 * e + 1]);
                     db[e] = pack_bf16x2(d0, d1);
-                    float h0, l0, h1, l1;
-                    split_bf16(d0 * g_dec[i0], h0, l0);
-                    split_bf16(d1 * g_dec[i1], h1, l1);
-                    dh[e] = pack_bf16x2(h0, h1);
-                    dl[e] = pack_bf16x2(l0, l1);
+                    split2_bf16(d0 * g_dec[i0], d1 * g_dec[i1], dh[e], dl[e]);
                 }
                 tmem_st16(tmem_addr(tm, lane_base, TM_DBF + 16 * hs), db);
                 tmem_st16(tmem_addr(tm, lane_base, TM_DPH + 16 * hs), dh);
@@ -619,9 +599,9 @@ cudaError_t launch_prefill_tc(const PrefillArgs &p, void *workspace, cudaStream_
     if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
     const int64_t units = tc_num_slots(p.total_tokens, p.num_seqs) * p.Hv;
     char *ws = static_cast<char *>(workspace);
-    float *ws_T = reinterpret_cast<float *>(ws);
-    __nv_bfloat16 *ws_P = reinterpret_cast<__nv_bfloat16 *>(ws + units * kTcTileBytes);
-    float *ws_g = reinterpret_cast<float *>(ws + units * (kTcTileBytes + kTcPBytes));
+    uint8_t *ws_T = reinterpret_cast<uint8_t *>(ws);
+    __nv_bfloat16 *ws_P = reinterpret_cast<__nv_bfloat16 *>(ws + units * kTcTBytes);
+    float *ws_g = reinterpret_cast<float *>(ws + units * (kTcTBytes + kTcPBytes));
     CUtensorMap qm, km, vm;
     std::memset(&qm, 0, sizeof(qm));
     std::memset(&km, 0, sizeof(km));

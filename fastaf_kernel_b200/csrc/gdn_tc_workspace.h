@@ -9,12 +9,15 @@
 // so the workspace is sized from T and N alone, without reading cu_seqlens.
 //
 // Three arrays, each indexed by unit = slot * Hv + v-head:
-//   T  fp32 [64][64] row-major, T = (I + A)^-1 with zeros above the diagonal (16 KB);
-//   P  bf16 [64][64], P[i][j] = exp(gamma_i - gamma_j) q_i.k_j for j <= i, zero above,
-//      stored exactly as the tensor core reads it from shared memory: 128-byte rows
-//      with the 16-byte chunk index XOR-ed by (i & 7) (8 KB);
+//   T tiles: T' = T diag(beta) and T'' = T diag(beta Gamma), T = (I + A)^-1 (zero above
+//      the diagonal), each split into bf16 hi + lo: four bf16 [64][64] tiles in the
+//      order T'hi, T'lo, T''hi, T''lo (32 KB);
+//   P  bf16 [64][64], P[i][j] = exp(gamma_i - gamma_j) q_i.k_j for j <= i, zero above (8 KB);
 //   gates: four fp32 [64] rows: beta, gamma * log2(e), Gamma = exp(gamma),
 //      exp(gamma_63 - gamma) (1 KB).
+// Every bf16 tile is stored exactly as the tensor core reads it from shared memory
+// (K-major [i][j]): 128-byte rows with the 16-byte chunk index XOR-ed by (i & 7), so
+// one bulk copy moves it into place.
 // Padding tokens of a partial chunk have beta = 0 and log alpha = 0.
 #pragma once
 
@@ -22,10 +25,11 @@
 
 namespace gdn {
 
-constexpr int64_t kTcTileBytes = 64 * 64 * 4;
+constexpr int64_t kTcTileBytes = 64 * 64 * 2;          // one bf16 [64][64] tile
+constexpr int64_t kTcTBytes = 4 * kTcTileBytes;          // T'hi, T'lo, T''hi, T''lo
 constexpr int64_t kTcPBytes = 64 * 64 * 2;
 constexpr int64_t kTcGateBytes = 4 * 64 * 4;
-constexpr int64_t kTcUnitBytes = kTcTileBytes + kTcPBytes + kTcGateBytes;
+constexpr int64_t kTcUnitBytes = kTcTBytes + kTcPBytes + kTcGateBytes;
 
 __host__ __device__ inline int64_t tc_num_slots(int64_t total_tokens, int64_t num_seqs) {
     return (total_tokens + 63) / 64 + num_seqs;

@@ -115,8 +115,8 @@ GDN_API int gdn_prefill_ws(const void *q, const void *k, const void *v, const fl
  * no driver allocation allowed on a latency-critical path, or memory accounting that
  * forbids allocations outside their allocator).  Same arguments and contract as
  * gdn_prefill; additionally requires
- *   (ceil(total_tokens / 64) + num_seqs) * num_v_heads * 25600 <= 64 MiB
- * (e.g. 4608 tokens in up to 8 sequences with 32 v-heads) and total_tokens >= 64;
+ *   (ceil(total_tokens / 64) + num_seqs) * num_v_heads * 41984 <= 64 MiB
+ * (e.g. 2560 tokens in up to 9 sequences with 32 v-heads) and total_tokens >= 64;
  * larger calls return GDN_ERR_INVALID_ARGUMENT before any launch.  The first call on
  * each device resolves the array's address (cudaGetSymbolAddress with that device
  * current); make that first call before any stream capture that would include it.
@@ -137,7 +137,7 @@ GDN_API int gdn_prefill_noalloc(const void *q, const void *k, const void *v, con
 GDN_API int gdn_prefill_resolve(int64_t total_tokens, int method);
 
 /* Workspace bytes gdn_prefill_ws needs for GDN_PREFILL_TCGEN05:
- * (ceil(total_tokens / 64) + num_seqs) * num_v_heads * 25600.  No counterpart in the reference. */
+ * (ceil(total_tokens / 64) + num_seqs) * num_v_heads * 41984.  No counterpart in the reference. */
 GDN_API size_t gdn_prefill_workspace_size(int64_t num_seqs, int64_t total_tokens, int num_v_heads);
 
 /*

@@ -200,7 +200,7 @@ def test_prefill_caller_workspace():
     lib = _lib.load()
     T, N = g["q"].shape[0], 3
     nbytes = lib.gdn_prefill_workspace_size(N, T, 8)
-    assert nbytes == ((T + 63) // 64 + N) * 8 * 25600
+    assert nbytes == ((T + 63) // 64 + N) * 8 * 41984
     ws = torch.full((nbytes // 4,), float("nan"), device=DEV)
     out = torch.empty_like(o_ref)
     ns = torch.empty_like(s_ref)
