@@ -69,13 +69,14 @@ constexpr uint32_t OFF_T1H = 128 * 1024;    // 8 KB each, K-major [i][j] (from t
 constexpr uint32_t OFF_T1L = 136 * 1024;    //   T' = T diag(beta) hi/lo, T'' = T diag(beta Gamma) hi/lo
 constexpr uint32_t OFF_T2H = 144 * 1024;
 constexpr uint32_t OFF_T2L = 152 * 1024;
-constexpr uint32_t OFF_WH = 160 * 1024;     // 16 KB each: -W hi/lo, MN-major [k][i]
-constexpr uint32_t OFF_WL = 176 * 1024;
-constexpr uint32_t OFF_QS = 192 * 1024;     // 16 KB: diag(Gamma) Q, K-major [i][k]
+constexpr uint32_t OFF_WH = 160 * 1024;     // 16 KB each, MN-major [k][i]: -W hi, -W lo, (diag(Gamma) Q)^T;
+constexpr uint32_t OFF_WL = 176 * 1024;     //   one N = 192 operand of the delta batch
+constexpr uint32_t OFF_QS = 192 * 1024;
 constexpr uint32_t OFF_GST = 208 * 1024;    // 2 stages x 1 KB: beta, gamma*log2(e), Gamma, decay-to-end
 constexpr uint32_t SMEM_BYTES = 210 * 1024;
 static_assert(OFF_T1L - OFF_T1H == kTcTileBytes && OFF_T2H - OFF_T1H == 2 * kTcTileBytes,
-              "T tiles sit in shared memory in their workspace order");
+              "T tiles sit in shared memory in their workspace order (T'_hi rows 0-63 and T'_lo rows"
+              " 64-127 of one K-major N = 128 operand)");
 constexpr uint32_t kStageTx = 6 * 8192 + kTcPBytes + kTcGateBytes;
 
 // TMEM columns (all 512 allocated).
@@ -85,9 +86,12 @@ constexpr uint32_t TM_SLO = 192;  // [192,256) bf16x2 S lo | later delta' hi [16
 constexpr uint32_t TM_DBF = 128;
 constexpr uint32_t TM_DPH = 160;
 constexpr uint32_t TM_DPL = 192;
-constexpr uint32_t TM_U0 = 256;   // [256,384) two buffers: U^T, then delta^T (lanes v, columns i)
-constexpr uint32_t TM_W = 384;    // [384,448) W^T (lanes k, columns i)
-constexpr uint32_t TM_O = 448;    // [448,512) (Gamma Q S^T)^T, then O^T
+constexpr uint32_t TM_W = 256;    // [256,320) W^T (lanes k, columns i)
+// The U batch writes [U | X] and the delta batch accumulates into [U | X | O] (lanes v,
+// columns i); delta^T = U + X:
+constexpr uint32_t TM_U = 320;    // [320,384) (T'_hi V)^T - S_hi W_hi^T - S_lo W_hi^T
+constexpr uint32_t TM_X = 384;    // [384,448) (T'_lo V)^T - S_hi W_lo^T
+constexpr uint32_t TM_O = 448;    // [448,512) (Gamma Q S_hi^T)^T, then O^T (zero before the batch)
 
 enum WaitSite { kWaitTma = 1, kWaitWU = 3, kWaitD = 4, kWaitS = 5, kWaitTT = 6,
                 kWaitW = 7, kWaitSS = 8, kWaitDS = 9, kWaitT = 10, kWaitIssue = 11, kWaitUD = 12 };
@@ -233,11 +237,12 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             const uint64_t dV0 = smem_desc_sw128(sbase + OFF_V, 8192, 1024);
             const uint64_t dT1h = smem_desc_sw128(sbase + OFF_T1H, 16, 1024);
             const uint64_t dT2h = smem_desc_sw128(sbase + OFF_T2H, 16, 1024);
-            const uint64_t dWh = smem_desc_sw128(sbase + OFF_WH, 8192, 1024);
-            const uint64_t dQS = smem_desc_sw128(sbase + OFF_QS, 16, 1024);
+            // [-W hi | -W lo | (Gamma Q)^T]: three MN-major 64-column atoms 16 KB apart
+            static_assert(OFF_WL - OFF_WH == 16384 && OFF_QS - OFF_WL == 16384, "N = 192 operand layout");
+            const uint64_t dWh = smem_desc_sw128(sbase + OFF_WH, 16384, 1024);
             const uint64_t dP0 = smem_desc_sw128(sbase + OFF_P, 16, 1024);
             // (the lo tiles sit 8 or 16 KB above the hi tiles; stage 1 one stage above stage 0)
-            constexpr uint64_t kLoT = (OFF_T1L - OFF_T1H) >> 4, kLoW = (OFF_WL - OFF_WH) >> 4;
+            constexpr uint64_t kLoT = (OFF_T1L - OFF_T1H) >> 4;
             static_assert(OFF_T2L - OFF_T2H == OFF_T1L - OFF_T1H, "T' / T'' hi-lo spacing");
             constexpr uint32_t id6 = idesc_bf16_f32(128, 64, true, false);
             auto mma6w = [&](int c) {   // W^T = K^T T''^T -> TM_W
@@ -249,29 +254,20 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                                id6, part | s);
                 mma_commit(b_wdone);
             };
-            auto mma6u = [&](int c) {   // U^T = V^T T'^T -> TM_U[c & 1]
+            auto mma6u = [&](int c) {   // [U | X] = V^T [T'_hi | T'_lo]^T (the two tiles as one N = 128 operand)
+                constexpr uint32_t id128 = idesc_bf16_f32(128, 128, true, false);
 #pragma unroll
-                for (int part = 0; part < 2; ++part)
-#pragma unroll
-                    for (int s = 0; s < 4; ++s)
-                        mma_ss(tm + TM_U0 + (c & 1) * 64, dV0 + (c & 1) * (V_STAGE >> 4) + 128 * s,
-                               dT1h + part * kLoT + 2 * s, id6, part | s);
+                for (int s = 0; s < 4; ++s)
+                    mma_ss(tm + TM_U, dV0 + (c & 1) * (V_STAGE >> 4) + 128 * s, dT1h + 2 * s, id128, s);
                 mma_commit(b_udone);
             };
-            auto mma8 = [&](int c) {    // delta^T = U^T - S W^T -> TM_U[c & 1]; (Gamma Q S^T)^T -> TM_O
-                const uint32_t tu = TM_U0 + (c & 1) * 64;
-                constexpr uint32_t idw = idesc_bf16_f32(128, 64, false, true);
+            auto mma8 = [&](int) {      // [U | X | O] += S_hi [-W_hi | -W_lo | Gamma Q]^T;  U += S_lo (-W_hi)^T
+                constexpr uint32_t id192 = idesc_bf16_f32(128, 192, false, true);
+                constexpr uint32_t id64 = idesc_bf16_f32(128, 64, false, true);
 #pragma unroll
-                for (int part = 0; part < 3; ++part) {
-                    const uint32_t src = part == 1 ? TM_SLO : TM_SHI;
+                for (int s = 0; s < 8; ++s) mma_ts(tm + TM_U, tm + TM_SHI + 8 * s, dWh + 128 * s, id192, 1);
 #pragma unroll
-                    for (int s = 0; s < 8; ++s)
-                        mma_ts(tm + tu, tm + src + 8 * s, dWh + (part == 2 ? kLoW : 0) + 128 * s, idw, 1);
-                }
-                constexpr uint32_t idq = idesc_bf16_f32(128, 64, false, false);
-#pragma unroll
-                for (int s = 0; s < 8; ++s)
-                    mma_ts(tm + TM_O, tm + TM_SHI + 8 * s, dQS + (s >> 2) * 512 + (s & 3) * 2, idq, s > 0);
+                for (int s = 0; s < 8; ++s) mma_ts(tm + TM_U, tm + TM_SLO + 8 * s, dWh + 128 * s, id64, 1);
                 mma_commit(b_d);
             };
             auto mma10 = [&](int c) {   // S += delta'^T K, O^T += delta^T P^T
@@ -397,6 +393,12 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             tmem_ld32(tmem_addr(tm, lane_base, TM_O), *reinterpret_cast<uint32_t(*)[32]>(o));
             tmem_ld32(tmem_addr(tm, lane_base, TM_O + 32), *reinterpret_cast<uint32_t(*)[32]>(o + 32));
             tmem_wait_ld_dep(o);
+            {
+                const uint32_t z[32] = {};   // the next delta batch accumulates into O^T
+                tmem_st32(tmem_addr(tm, lane_base, TM_O), z);
+                tmem_st32(tmem_addr(tm, lane_base, TM_O + 32), z);
+                tmem_wait_st();
+            }
             tc_fence_before();
             warp_arrive(b_oread, lane);
             const int64_t t0 = s0 + static_cast<int64_t>(c) * kC;
@@ -422,19 +424,30 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             // diag(Gamma) Q once the previous chunk's Q S^T product has read the tile
             if (c > 0 && !wait_warp(b_d, (c - 1) & 1, kWaitD, abort)) break;
             {
-                const uint8_t *src = sm + OFF_KQ + st * KQ_STAGE + 8192;
+                // (diag(Gamma) Q)^T, MN-major [k][i]: thread pt = k reads column k of the Q
+                // tile (two threads per 4-byte word, conflict-free) and writes row k.
+                const uint8_t *src = sm + OFF_KQ + st * KQ_STAGE + 8192 + (pt >> 6) * 16384 + (pt & 7) * 2;
+                const int kc = (pt & 63) >> 3;
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const int idx = pt + 128 * u, half = idx >> 9, i = (idx >> 3) & 63, ch = idx & 7;
-                    const uint32_t off = half * 16384 + sw128(i, ch);
-                    const uint4 x = *reinterpret_cast<const uint4 *>(src + off);
-                    const float gi = g_Gam[i];
-                    uint32_t w[4] = {x.x, x.y, x.z, x.w};
+                for (int ch = 0; ch < 8; ++ch) {
+                    uint32_t w[4];
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) w[e] = pack_bf16x2(bf16_lo(w[e]) * gi, bf16_hi(w[e]) * gi);
-                    *reinterpret_cast<uint4 *>(sm + OFF_QS + half * 8192 + sw128(i, ch)) =
-                        make_uint4(w[0], w[1], w[2], w[3]);
+                    for (int e = 0; e < 4; ++e) {
+                        const int i = ch * 8 + 2 * e;
+                        const float q0 = __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(src + sw128(i, kc)));
+                        const float q1 =
+                            __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(src + sw128(i + 1, kc)));
+                        w[e] = pack_bf16x2(q0 * g_Gam[i], q1 * g_Gam[i + 1]);
+                    }
+                    *reinterpret_cast<uint4 *>(sm + OFF_QS + sw128(pt, ch)) = make_uint4(w[0], w[1], w[2], w[3]);
                 }
+            }
+            if (c == 0) {
+                // The delta batch accumulates into O^T: start from zero.
+                const uint32_t z[32] = {};
+                tmem_st32(tmem_addr(tm, lane_base, TM_O), z);
+                tmem_st32(tmem_addr(tm, lane_base, TM_O + 32), z);
+                tmem_wait_st();
             }
             fence_proxy_async_smem();
             tc_fence_before();
@@ -523,14 +536,16 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             // delta (fp32, TMEM) -> bf16 (output path) and exp(gamma_63 - gamma_i) delta -> hi/lo
             if (!(ok = wait_warp(b_d, c & 1, kWaitD, abort))) break;
             {
-                const uint32_t tu = TM_U0 + st * 64;
-                uint32_t r[32], db[16], dh[16], dl[16];
-                tmem_ld32(tmem_addr(tm, lane_base, tu + 32 * hs), r);
+                uint32_t r[32], x[32], db[16], dh[16], dl[16];
+                tmem_ld32(tmem_addr(tm, lane_base, TM_U + 32 * hs), r);
+                tmem_ld32(tmem_addr(tm, lane_base, TM_X + 32 * hs), x);
                 tmem_wait_ld_dep(r);
+                tmem_wait_ld_dep(x);
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
                     const int i0 = hs * 32 + 2 * e, i1 = i0 + 1;
-                    const float d0 = __uint_as_float(r[2 * e]), d1 = __uint_as_float(r[2 * e + 1]);
+                    const float d0 = __uint_as_float(r[2 * e]) + __uint_as_float(x[2 * e]);
+                    const float d1 = __uint_as_float(r[2 * e + 1]) + __uint_as_float(x[2 * e + 1]);
                     db[e] = pack_bf16x2(d0, d1);
                     split2_bf16(d0 * g_dec[i0], d1 * g_dec[i1], dh[e], dl[e]);
                 }
