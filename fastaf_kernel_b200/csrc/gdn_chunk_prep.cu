@@ -13,12 +13,15 @@
 // the chain kernel keeps only the state path on its serial critical path.
 //
 // The work of one chunk is a chain of short dependent steps, so the kernel is built
-// for many chunks in flight per SM: CTAs of 4 warps with ~54 KB of shared memory
-// (4 per SM), each handling chunks g, g + G, g + 2G, ... of one (sequence, v-head).
-// Warp w owns rows 16w..16w+15 of the chunk:
-//   * K K^T and Q K^T on mma.sync (bf16 inputs are exact, fp32 accumulation); A stays
-//     in the accumulator registers that computed it, its 16x16 diagonal block also
-//     goes to shared memory in fp32, P goes to the workspace as bf16;
+// for many chunks in flight per SM: CTAs of 4 warps with ~55 KB of shared memory
+// (4 per SM), each handling chunks g, g + G, g + 2G, ... of one sequence and NH v-heads
+// that share a q/k head (NH = 2 when the number of v-heads per q/k head is even, else 1):
+// K K^T, Q K^T and the K/Q tile loads, which depend only on the q/k head, are done once
+// for the NH v-heads.  Warp w owns rows 16w..16w+15 of the chunk:
+//   * K K^T and Q K^T on mma.sync (bf16 inputs are exact, fp32 accumulation); K K^T stays
+//     in the accumulator registers that computed it and each v-head's A is formed from
+//     it in registers, its 16x16 diagonal block also goes to shared memory in fp32; each
+//     v-head's P goes from the Q K^T registers to the workspace as bf16;
 //   * the four diagonal blocks D_b = (I + A_bb)^-1 by fp32 forward substitution;
 //   * then, block-recursively on mma.sync with every fp32 operand split into bf16
 //     hi + lo (hi*hi + hi*lo + lo*hi):
@@ -51,8 +54,9 @@ constexpr uint32_t OFF_SL = 24576;
 constexpr uint32_t OFF_TH = 32768;                  // bf16 [64][64] T hi/lo, 128-byte swizzled rows
 constexpr uint32_t OFF_TL = 40960;
 constexpr uint32_t OFF_AD = 49152;                  // fp32 diagonal blocks of A: 4 x [16][17]
-constexpr uint32_t OFF_GATE = OFF_AD + 4 * 16 * 17 * 4;   // beta, gamma*log2(e), Gamma, decay-to-end
-constexpr uint32_t SMEM_BYTES = OFF_GATE + 4 * 64 * 4;
+constexpr uint32_t OFF_GATE = OFF_AD + 4 * 16 * 17 * 4;   // per v-head: beta, gamma*log2(e), Gamma, decay-to-end
+constexpr uint32_t kGateBytes = 4 * 64 * 4;
+constexpr uint32_t smem_bytes(int nh) { return OFF_GATE + nh * kGateBytes; }
 
 struct PrepParams {
     const __nv_bfloat16 *q, *k;
@@ -139,14 +143,16 @@ __device__ __forceinline__ void store_block(const float (&acc)[NT][4], float sgn
         }
 }
 
+template <int NH>
 __global__ void __launch_bounds__(kThreads, 4) chunk_prep_kernel(const PrepParams p) {
     extern __shared__ __align__(1024) uint8_t sm[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t4 = lane & 3;
-    const int64_t chain = blockIdx.x;
-    const int64_t n = chain / p.Hv;
-    const int h = static_cast<int>(chain % p.Hv);
-    const int hq = h / (p.Hv / p.Hq);
+    const int64_t chain = blockIdx.x;                  // (sequence, group of NH v-heads)
+    const int hgroups = p.Hv / NH;
+    const int64_t n = chain / hgroups;
+    const int h0 = static_cast<int>(chain % hgroups) * NH;
+    const int hq = h0 / (p.Hv / p.Hq);
     int64_t s0 = p.cu_seqlens[n], s1 = p.cu_seqlens[n + 1];
     s0 = s0 < 0 ? 0 : (s0 > p.T ? p.T : s0);
     s1 = s1 < s0 ? s0 : (s1 > p.T ? p.T : s1);
@@ -156,14 +162,16 @@ __global__ void __launch_bounds__(kThreads, 4) chunk_prep_kernel(const PrepParam
     const uint32_t sbase = smem_addr(sm);
     float *A_d = reinterpret_cast<float *>(sm + OFF_AD);
     float *T_f = reinterpret_cast<float *>(sm + OFF_TF);
-    float *g_beta = reinterpret_cast<float *>(sm + OFF_GATE);
-    float *g_gam2 = g_beta + 64, *g_Gam = g_beta + 128, *g_dec = g_beta + 192;
-    const float exp_A = expf(load_scalar(p.A_log, h, p.param_dtype));
-    const float dtb = load_scalar(p.dt_bias, h, p.param_dtype);
+    // gate vectors of v-head h0 + hh: beta, gamma*log2(e), Gamma, decay-to-end
+    auto gates = [&](int hh) { return reinterpret_cast<float *>(sm + OFF_GATE + hh * kGateBytes); };
+    // warp hh < NH computes the gates of v-head h0 + hh
+    const int hw = h0 + (warp < NH ? warp : 0);
+    const float exp_A = expf(load_scalar(p.A_log, hw, p.param_dtype));
+    const float dtb = load_scalar(p.dt_bias, hw, p.param_dtype);
     const uint32_t Th = sbase + OFF_TH, Tl = sbase + OFF_TL, Sh = sbase + OFF_SH, Sl = sbase + OFF_SL;
     const int r0 = 16 * warp;    // this warp's rows of the chunk
 
-    // Warp 0 keeps the next chunk's gate inputs in registers (loaded a chunk ahead).
+    // Warps 0..NH-1 keep the next chunk's gate inputs in registers (loaded a chunk ahead).
     float ga[2] = {0.f, 0.f}, gb[2] = {0.f, 0.f};
     auto fetch_gates = [&](int cc) {
         const int64_t tb = s0 + static_cast<int64_t>(cc) * kC;
@@ -171,12 +179,12 @@ __global__ void __launch_bounds__(kThreads, 4) chunk_prep_kernel(const PrepParam
         for (int u = 0; u < 2; ++u) {
             const int64_t t = tb + lane + 32 * u;
             if (t < s1) {
-                ga[u] = load_scalar(p.a, t * p.Hv + h, p.gate_dtype);
-                gb[u] = load_scalar(p.b, t * p.Hv + h, p.gate_dtype);
+                ga[u] = load_scalar(p.a, t * p.Hv + hw, p.gate_dtype);
+                gb[u] = load_scalar(p.b, t * p.Hv + hw, p.gate_dtype);
             }
         }
     };
-    if (warp == 0) fetch_gates(blockIdx.y);
+    if (warp < NH) fetch_gates(blockIdx.y);
 
     for (int c = blockIdx.y; c < nch; c += p.groups) {
         const int64_t t0 = s0 + static_cast<int64_t>(c) * kC;
@@ -185,8 +193,8 @@ __global__ void __launch_bounds__(kThreads, 4) chunk_prep_kernel(const PrepParam
         load_tile(sbase + OFF_Q, p.q, p.T, p.Hq, hq, t0, tid);
         cp_async_commit();
 
-        // Gates (warp 0), then the next chunk's inputs.
-        if (warp == 0) {
+        // Gates (warp hh for v-head h0 + hh), then the next chunk's inputs.
+        if (warp < NH) {
             float lg[2], bt[2];
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
@@ -205,6 +213,7 @@ __global__ void __launch_bounds__(kThreads, 4) chunk_prep_kernel(const PrepParam
             x1 += __shfl_sync(0xffffffffu, x0, 31);
             const float xC = __shfl_sync(0xffffffffu, x1, 31);
             constexpr float kLog2e = 1.4426950408889634f;
+            float *g_beta = gates(warp), *g_gam2 = g_beta + 64, *g_Gam = g_beta + 128, *g_dec = g_beta + 192;
             g_beta[lane] = bt[0]; g_beta[lane + 32] = bt[1];
             g_gam2[lane] = x0 * kLog2e; g_gam2[lane + 32] = x1 * kLog2e;
             g_Gam[lane] = expf(x0); g_Gam[lane + 32] = expf(x1);
@@ -214,12 +223,11 @@ __global__ void __launch_bounds__(kThreads, 4) chunk_prep_kernel(const PrepParam
         __syncthreads();
 
         // K K^T rows r0..r0+15 (columns right of the diagonal block are zero in A and
-        // skipped); A = beta_i exp(gamma_i - gamma_j) k_i.k_j for j < i stays in these
-        // registers, its diagonal block also goes to A_d (fp32).
-        float A[8][4];
+        // skipped), kept in these registers for the NH v-heads.
+        float R[8][4];
         {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) A[i][0] = A[i][1] = A[i][2] = A[i][3] = 0.0f;
+            for (int i = 0; i < 8; ++i) R[i][0] = R[i][1] = R[i][2] = R[i][3] = 0.0f;
             const uint32_t sK = sbase + OFF_K;
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) {
@@ -230,29 +238,14 @@ __global__ void __launch_bounds__(kThreads, 4) chunk_prep_kernel(const PrepParam
                     if (16 * np > r0) continue;
                     uint32_t bf[4];
                     ldsm_x4(bf, b_addr_nk<256>(sK, np * 16, kk * 16, lane));
-                    mma16816(A[2 * np], af, bf[0], bf[1]);
-                    mma16816(A[2 * np + 1], af, bf[2], bf[3]);
-                }
-            }
-#pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
-                const int i = r0 + g + 8 * hf;
-                const float gi = g_gam2[i], bi = g_beta[i];
-#pragma unroll
-                for (int ntl = 0; ntl < 8; ++ntl) {
-#pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        const int j = ntl * 8 + 2 * t4 + u;
-                        const float a = j < i ? bi * exp2f(gi - g_gam2[j]) * A[ntl][2 * hf + u] : 0.0f;
-                        A[ntl][2 * hf + u] = a;
-                        if ((j >> 4) == warp) A_d[(16 * warp + (i & 15)) * 17 + (j & 15)] = a;
-                    }
+                    mma16816(R[2 * np], af, bf[0], bf[1]);
+                    mma16816(R[2 * np + 1], af, bf[2], bf[3]);
                 }
             }
         }
-        // Q K^T rows r0.. -> P = exp(gamma_i - gamma_j) q_i.k_j for j <= i, to the workspace
-        // as bf16 in the swizzled layout the chain kernel's tensor core reads.
-        const int64_t unit = tc_slot(s0, c, n) * p.Hv + h;
+        // Q K^T rows r0.. -> P = exp(gamma_i - gamma_j) q_i.k_j for j <= i of each v-head, to
+        // the workspace as bf16 in the swizzled layout the chain kernel's tensor core reads.
+        const int64_t unit0 = tc_slot(s0, c, n) * p.Hv + h0;
         {
             float acc[8][4];
 #pragma unroll
@@ -271,17 +264,45 @@ __global__ void __launch_bounds__(kThreads, 4) chunk_prep_kernel(const PrepParam
                     mma16816(acc[2 * np + 1], af, bf[2], bf[3]);
                 }
             }
-            uint8_t *dP = reinterpret_cast<uint8_t *>(p.ws_P) + unit * kTcPBytes;
 #pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
-                const int i = r0 + g + 8 * hf;
-                const float gi = g_gam2[i];
+            for (int hh = 0; hh < NH; ++hh) {
+                const float *g_gam2 = gates(hh) + 64;
+                uint8_t *dP = reinterpret_cast<uint8_t *>(p.ws_P) + (unit0 + hh) * kTcPBytes;
 #pragma unroll
-                for (int ntl = 0; ntl < 8; ++ntl) {
-                    const int j = ntl * 8 + 2 * t4;
-                    const float p0 = j <= i ? exp2f(gi - g_gam2[j]) * acc[ntl][2 * hf] : 0.0f;
-                    const float p1 = j + 1 <= i ? exp2f(gi - g_gam2[j + 1]) * acc[ntl][2 * hf + 1] : 0.0f;
-                    *reinterpret_cast<uint32_t *>(dP + swz<128>(i, j)) = pack_bf16x2(p0, p1);
+                for (int hf = 0; hf < 2; ++hf) {
+                    const int i = r0 + g + 8 * hf;
+                    const float gi = g_gam2[i];
+#pragma unroll
+                    for (int ntl = 0; ntl < 8; ++ntl) {
+                        const int j = ntl * 8 + 2 * t4;
+                        const float p0 = j <= i ? exp2f(gi - g_gam2[j]) * acc[ntl][2 * hf] : 0.0f;
+                        const float p1 = j + 1 <= i ? exp2f(gi - g_gam2[j + 1]) * acc[ntl][2 * hf + 1] : 0.0f;
+                        *reinterpret_cast<uint32_t *>(dP + swz<128>(i, j)) = pack_bf16x2(p0, p1);
+                    }
+                }
+            }
+        }
+
+#pragma unroll 1
+        for (int hh = 0; hh < NH; ++hh) {
+        const float *g_beta = gates(hh), *g_gam2 = g_beta + 64, *g_Gam = g_beta + 128;
+        const int64_t unit = unit0 + hh;
+        // A = beta_i exp(gamma_i - gamma_j) k_i.k_j for j < i in registers (in place of
+        // K K^T when this is its only v-head); its diagonal block also goes to A_d (fp32).
+        float A2[8][4];
+        float(&A)[8][4] = NH == 1 ? R : A2;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+            const int i = r0 + g + 8 * hf;
+            const float gi = g_gam2[i], bi = g_beta[i];
+#pragma unroll
+            for (int ntl = 0; ntl < 8; ++ntl) {
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int j = ntl * 8 + 2 * t4 + u;
+                    const float a = j < i ? bi * exp2f(gi - g_gam2[j]) * R[ntl][2 * hf + u] : 0.0f;
+                    A[ntl][2 * hf + u] = a;
+                    if ((j >> 4) == warp) A_d[(16 * warp + (i & 15)) * 17 + (j & 15)] = a;
                 }
             }
         }
@@ -391,7 +412,8 @@ __global__ void __launch_bounds__(kThreads, 4) chunk_prep_kernel(const PrepParam
         }
         p.ws_g[unit * (kTcGateBytes / 4) + tid] = g_beta[tid];
         p.ws_g[unit * (kTcGateBytes / 4) + 128 + tid] = g_beta[128 + tid];
-        __syncthreads();   // the next chunk's copies overwrite T_f and the tiles
+        __syncthreads();   // the next v-head, or the next chunk's copies, overwrite T_f and the tiles
+        }
     }
 }
 
@@ -406,17 +428,20 @@ int prep_groups(int64_t chains) {
 
 cudaError_t launch_chunk_prep(const PrefillArgs &p, uint8_t *ws_T, __nv_bfloat16 *ws_P, float *ws_g,
                               cudaStream_t stream) {
-    const int64_t chains = p.num_seqs * p.Hv;
+    // Two v-heads per CTA when the v-heads of every q/k head pair up.
+    const int nh = ((p.Hv / p.Hq) % 2 == 0) ? 2 : 1;
+    const int64_t chains = p.num_seqs * (p.Hv / nh);
     if (chains == 0) return cudaSuccess;
     if (chains > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
     const int groups = prep_groups(chains);
-    cudaError_t e = cudaFuncSetAttribute(chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         SMEM_BYTES);
+    auto kernel = nh == 2 ? chunk_prep_kernel<2> : chunk_prep_kernel<1>;
+    const uint32_t smem = smem_bytes(nh);
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     PrepParams pp{static_cast<const __nv_bfloat16 *>(p.q), static_cast<const __nv_bfloat16 *>(p.k), p.A_log,
                   p.a, p.dt_bias, p.b, p.cu_seqlens, p.total_tokens, p.Hq, p.Hv, groups, p.gate_dtype,
                   p.param_dtype, ws_T, ws_g, ws_P};
-    chunk_prep_kernel<<<dim3(static_cast<unsigned>(chains), groups), kThreads, SMEM_BYTES, stream>>>(pp);
+    kernel<<<dim3(static_cast<unsigned>(chains), groups), kThreads, smem, stream>>>(pp);
     return cudaGetLastError();
 }
 
