@@ -27,10 +27,13 @@ GDN_PREFILL_CHUNKED = 1
 GDN_PREFILL_RECURRENT = 2
 GDN_PREFILL_TCGEN05 = 3
 
+GDN_FLAG_QK_L2NORM = 1
+
 # Every symbol include/gdn_b200.h declares.
 EXPORTED_SYMBOLS = ("gdn_prefill", "gdn_prefill_ex", "gdn_prefill_ws", "gdn_prefill_workspace_size",
-                    "gdn_prefill_resolve", "gdn_prefill_noalloc",
-                    "gdn_decode", "gdn_device_status", "gdn_last_error", "gdn_version")
+                    "gdn_prefill_resolve", "gdn_prefill_noalloc", "gdn_prefill_flags",
+                    "gdn_decode", "gdn_decode_flags", "gdn_device_status", "gdn_last_error",
+                    "gdn_version")
 
 _lock = threading.Lock()
 _lib = None
@@ -80,6 +83,11 @@ def load() -> ctypes.CDLL:
         lib.gdn_decode.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i64, i32, i32, i32, f32,
                                    i32, i32, vp, vp, vp]
         lib.gdn_decode.restype = i32
+        lib.gdn_decode_flags.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i64, i32, i32, i32, f32,
+                                         i32, i32, vp, vp, i32, vp]
+        lib.gdn_decode_flags.restype = i32
+        lib.gdn_prefill_flags.argtypes = prefill_args + [i32, i32, vp]
+        lib.gdn_prefill_flags.restype = i32
         lib.gdn_device_status.argtypes = [vp]
         lib.gdn_device_status.restype = i32
         lib.gdn_last_error.argtypes = []

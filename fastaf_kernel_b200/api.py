@@ -13,7 +13,11 @@ unchanged:
   * ``kernel_decode(..., new_state=state)`` updates the state in place;
   * ``method=`` chooses the prefill kernel: "tcgen05" (chunk prep + chain kernels on
     the 5th-generation tensor cores), "chunked" (mma.sync), "recurrent" (CUDA cores)
-    or "auto" (what ``prefill_method`` reports).
+    or "auto" (what ``prefill_method`` reports);
+  * ``use_qk_l2norm=True`` L2-normalises every q and k head vector first,
+    x <- bf16(x / sqrt(sum x^2 + 1e-6)) in fp32 -- the normalisation Gated DeltaNet
+    layers apply before the recurrence (fused into the decode kernel; a pre-pass for
+    prefill).  Off by default: the reference never normalises.
 """
 
 from __future__ import annotations
@@ -90,7 +94,8 @@ def kernel(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: Optional[to
            A_log: torch.Tensor, a: torch.Tensor, dt_bias: torch.Tensor, b: torch.Tensor,
            cu_seqlens: torch.Tensor, scale: Optional[float], *,
            output: Optional[torch.Tensor] = None, new_state: Optional[torch.Tensor] = None,
-           method: str = "auto", validate: bool = True) -> Tuple[torch.Tensor, torch.Tensor]:
+           method: str = "auto", validate: bool = True,
+           use_qk_l2norm: bool = False) -> Tuple[torch.Tensor, torch.Tensor]:
     """Varlen Gated DeltaNet prefill (solution/triton/kernel.py:416-489).
 
     q, k [T, Hq, D] bf16; v [T, Hv, D] bf16; state [N, Hv, D, D] fp32 k-last or
@@ -154,10 +159,11 @@ def kernel(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: Optional[to
     lib = _lib.load()
     with torch.cuda.device(device):
         stream = torch.cuda.current_stream(device).cuda_stream
-        _lib.check(lib.gdn_prefill_ex(
+        _lib.check(lib.gdn_prefill_flags(
             _ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias),
             _ptr(b), _ptr(cu), N, T, Hq, Hv, D, scale, _GATE_DTYPES[a.dtype],
-            _GATE_DTYPES[A_log.dtype], _ptr(output), _ptr(new_state), _METHODS[method], stream))
+            _GATE_DTYPES[A_log.dtype], _ptr(output), _ptr(new_state), _METHODS[method],
+            _lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm else 0, stream))
     return output, new_state
 
 
@@ -165,7 +171,8 @@ def kernel_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                   state: Optional[torch.Tensor], A_log: torch.Tensor, a: torch.Tensor,
                   dt_bias: torch.Tensor, b: torch.Tensor, scale: Optional[float], *,
                   output: Optional[torch.Tensor] = None,
-                  new_state: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+                  new_state: Optional[torch.Tensor] = None,
+                  use_qk_l2norm: bool = False) -> Tuple[torch.Tensor, torch.Tensor]:
     """Single-token Gated DeltaNet decode (solution/triton/kernel.py:492-556).
 
     q, k [B, 1, Hq, D] bf16; v [B, 1, Hv, D] bf16; a, b [B, 1, Hv];
@@ -220,10 +227,11 @@ def kernel_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     lib = _lib.load()
     with torch.cuda.device(device):
         stream = torch.cuda.current_stream(device).cuda_stream
-        _lib.check(lib.gdn_decode(
+        _lib.check(lib.gdn_decode_flags(
             _ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias),
             _ptr(b), B, Hq, Hv, D, scale, _GATE_DTYPES[a.dtype], _GATE_DTYPES[A_log.dtype],
-            _ptr(output), _ptr(new_state), stream))
+            _ptr(output), _ptr(new_state), _lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm else 0,
+            stream))
     return output, new_state
 
 

@@ -117,7 +117,17 @@ int gdn_decode(const void *q, const void *k, const void *v, const float *state,
                int64_t batch, int num_qk_heads, int num_v_heads, int head_size, float scale,
                int gate_dtype, int param_dtype, void *output, float *new_state,
                void *stream) {
+    return gdn_decode_flags(q, k, v, state, A_log, a, dt_bias, b, batch, num_qk_heads, num_v_heads,
+                            head_size, scale, gate_dtype, param_dtype, output, new_state, 0, stream);
+}
+
+int gdn_decode_flags(const void *q, const void *k, const void *v, const float *state,
+                     const void *A_log, const void *a, const void *dt_bias, const void *b,
+                     int64_t batch, int num_qk_heads, int num_v_heads, int head_size, float scale,
+                     int gate_dtype, int param_dtype, void *output, float *new_state, int flags,
+                     void *stream) {
     g_last_error[0] = '\0';
+    if (flags & ~GDN_FLAG_QK_L2NORM) return fail(GDN_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
     int rc = check_common(num_qk_heads, num_v_heads, head_size, gate_dtype, param_dtype, q, k, v,
                           A_log, a, dt_bias, b, output, new_state);
     if (rc) return rc;
@@ -132,7 +142,7 @@ int gdn_decode(const void *q, const void *k, const void *v, const float *state,
     if (batch == 0) return GDN_OK;
     gdn::DecodeArgs p{q, k, v, state, A_log, a, dt_bias, b, batch, num_qk_heads, num_v_heads,
                       scale == 0.0f ? 1.0f / sqrtf(static_cast<float>(head_size)) : scale,
-                      gate_dtype, param_dtype, output, new_state};
+                      gate_dtype, param_dtype, output, new_state, (flags & GDN_FLAG_QK_L2NORM) ? 1 : 0};
     return cuda_status(gdn::launch_decode(p, static_cast<cudaStream_t>(stream)), "gdn_decode launch");
 }
 
@@ -141,8 +151,10 @@ static int prefill_impl(const void *q, const void *k, const void *v, const float
                         const int32_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
                         int num_qk_heads, int num_v_heads, int head_size, float scale,
                         int gate_dtype, int param_dtype, void *output, float *new_state,
-                        int method, void *workspace, size_t workspace_bytes, void *stream) {
+                        int method, void *workspace, size_t workspace_bytes, void *stream,
+                        int flags = 0) {
     g_last_error[0] = '\0';
+    if (flags & ~GDN_FLAG_QK_L2NORM) return fail(GDN_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
     int rc = check_common(num_qk_heads, num_v_heads, head_size, gate_dtype, param_dtype, q, k, v,
                           A_log, a, dt_bias, b, output, new_state);
     if (rc) return rc;
@@ -168,6 +180,27 @@ static int prefill_impl(const void *q, const void *k, const void *v, const float
                        scale == 0.0f ? 1.0f / sqrtf(static_cast<float>(head_size)) : scale,
                        gate_dtype, param_dtype, output, new_state};
     const auto s = static_cast<cudaStream_t>(stream);
+    if (flags & GDN_FLAG_QK_L2NORM) {
+        // Normalised q and k into pool scratch, then the prefill on them.
+        const size_t qk_bytes = static_cast<size_t>(total_tokens) * num_qk_heads * head_size * 2;
+        if (qk_bytes == 0)
+            return prefill_impl(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs, total_tokens,
+                                num_qk_heads, num_v_heads, head_size, scale, gate_dtype, param_dtype, output,
+                                new_state, method, workspace, workspace_bytes, stream, 0);
+        void *qk = nullptr;
+        cudaError_t e = pool_alloc(&qk, 2 * qk_bytes, s);
+        if (e != cudaSuccess) return cuda_status(e, "gdn_prefill (qk l2norm) scratch");
+        void *qn = qk, *kn = static_cast<char *>(qk) + qk_bytes;
+        e = gdn::launch_qk_l2norm(q, k, total_tokens * num_qk_heads, qn, kn, s);
+        int rc2 = e != cudaSuccess ? cuda_status(e, "gdn_prefill (qk l2norm) launch")
+                                   : prefill_impl(qn, kn, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs,
+                                                  total_tokens, num_qk_heads, num_v_heads, head_size, scale,
+                                                  gate_dtype, param_dtype, output, new_state, method, workspace,
+                                                  workspace_bytes, stream, 0);
+        const cudaError_t ef = cudaFreeAsync(qk, s);
+        if (rc2 != GDN_OK) return rc2;
+        return cuda_status(ef, "gdn_prefill (qk l2norm) scratch release");
+    }
     // auto: the tcgen05 pipeline for large batches; below ~2K tokens its extra prep
     // launch does not pay off and the single-launch mma.sync kernel is faster.
     if (method == GDN_PREFILL_AUTO && gdn_prefill_resolve(total_tokens, method) == GDN_PREFILL_TCGEN05)
@@ -208,6 +241,17 @@ int gdn_prefill_ex(const void *q, const void *k, const void *v, const float *sta
     return prefill_impl(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs, total_tokens,
                         num_qk_heads, num_v_heads, head_size, scale, gate_dtype, param_dtype, output,
                         new_state, method, nullptr, 0, stream);
+}
+
+int gdn_prefill_flags(const void *q, const void *k, const void *v, const float *state,
+                      const void *A_log, const void *a, const void *dt_bias, const void *b,
+                      const int32_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
+                      int num_qk_heads, int num_v_heads, int head_size, float scale,
+                      int gate_dtype, int param_dtype, void *output, float *new_state,
+                      int method, int flags, void *stream) {
+    return prefill_impl(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs, total_tokens,
+                        num_qk_heads, num_v_heads, head_size, scale, gate_dtype, param_dtype, output,
+                        new_state, method, nullptr, 0, stream, flags);
 }
 
 int gdn_prefill_ws(const void *q, const void *k, const void *v, const float *state,

@@ -12,6 +12,12 @@
 //   S[v, :] = (S' - k u) + k vn           (:82-84)
 //   o[v] = scale * q . S[v, :]            (:86-87)
 //
+// Optionally (qk_l2norm) q and k are first L2-normalised per head, the usual step
+// before the recurrence in Gated DeltaNet layers (the reference never normalises and
+// its benchmark inputs arrive normalised): x <- bf16(x / sqrt(sum x^2 + 1e-6)), in
+// fp32 from the bf16 inputs, rounded back to bf16 as an upstream normalisation layer
+// would emit it.
+//
 // The step is HBM-bound (128 KiB of state traffic per (sequence, v-head)
 // against ~0.8 KiB of q/k/v/o), so the design goal is a copy-like access pattern: every 8 consecutive
 // lanes own one 512-byte state row, lane j holding the four float4 at columns
@@ -21,10 +27,24 @@
 
 namespace gdn {
 
+// L2-normalise a 128-element vector held by an aligned group of 8 lanes, 16 values per
+// lane: sum of squares per lane in index order, then a butterfly over the 8 lanes.
+__device__ __forceinline__ void l2norm_8lanes(float (&x)[16]) {
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) ss = fmaf(x[i], x[i], ss);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+    const float inv = 1.0f / sqrtf(ss + 1e-6f);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) x[i] = __bfloat162float(__float2bfloat16_rn(x[i] * inv));
+}
+
 constexpr int kDecodeThreads = 256;            // 32 rows per pass (8 lanes per row)
 constexpr int kRowsPerPass = kDecodeThreads / 8;
 
-template <int ROWS_PER_THREAD>
+template <int ROWS_PER_THREAD, bool QK_L2NORM>
 __global__ void __launch_bounds__(kDecodeThreads)
 decode_kernel(const __nv_bfloat16 *__restrict__ q, const __nv_bfloat16 *__restrict__ k,
               const __nv_bfloat16 *__restrict__ v, const float *state, const void *A_log,
@@ -59,6 +79,10 @@ decode_kernel(const __nv_bfloat16 *__restrict__ q, const __nv_bfloat16 *__restri
             kf[4 * m + 2] = bf16_lo(kk.y); kf[4 * m + 3] = bf16_hi(kk.y);
             qf[4 * m + 0] = bf16_lo(qq.x); qf[4 * m + 1] = bf16_hi(qq.x);
             qf[4 * m + 2] = bf16_lo(qq.y); qf[4 * m + 3] = bf16_hi(qq.y);
+        }
+        if (QK_L2NORM) {
+            l2norm_8lanes(kf);
+            l2norm_8lanes(qf);
         }
     }
 
@@ -127,14 +151,53 @@ cudaError_t launch_decode(const DecodeArgs &p, cudaStream_t stream) {
     const auto *k = static_cast<const __nv_bfloat16 *>(p.k);
     const auto *v = static_cast<const __nv_bfloat16 *>(p.v);
     auto *o = static_cast<__nv_bfloat16 *>(p.out);
-    if (rows_per_thread == 2)
-        decode_kernel<2><<<grid, kDecodeThreads, 0, stream>>>(
-            q, k, v, p.state, p.A_log, p.a, p.dt_bias, p.b, p.Hq, p.Hv, p.scale, p.gate_dtype,
-            p.param_dtype, o, p.new_state);
-    else
-        decode_kernel<1><<<grid, kDecodeThreads, 0, stream>>>(
-            q, k, v, p.state, p.A_log, p.a, p.dt_bias, p.b, p.Hq, p.Hv, p.scale, p.gate_dtype,
-            p.param_dtype, o, p.new_state);
+    auto kernel = rows_per_thread == 2 ? (p.qk_l2norm ? decode_kernel<2, true> : decode_kernel<2, false>)
+                                       : (p.qk_l2norm ? decode_kernel<1, true> : decode_kernel<1, false>);
+    kernel<<<grid, kDecodeThreads, 0, stream>>>(q, k, v, p.state, p.A_log, p.a, p.dt_bias, p.b, p.Hq, p.Hv,
+                                                p.scale, p.gate_dtype, p.param_dtype, o, p.new_state);
+    return cudaGetLastError();
+}
+
+// One 8-lane group per 128-element vector (4 per warp), the layout of the decode
+// kernel, so both produce the same bits.
+__global__ void __launch_bounds__(256) qk_l2norm_kernel(const __nv_bfloat16 *__restrict__ q,
+                                                        const __nv_bfloat16 *__restrict__ k, int64_t rows,
+                                                        __nv_bfloat16 *__restrict__ qn,
+                                                        __nv_bfloat16 *__restrict__ kn) {
+    const int64_t vec = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 3;
+    const int lane8 = threadIdx.x & 7;
+    const bool is_k = vec >= rows;
+    const int64_t r0 = is_k ? vec - rows : vec;
+    // Groups past the end compute on row 0 and store nothing: every lane stays for the
+    // full-warp shuffles.
+    const bool live = r0 < rows;
+    const int64_t r = live ? r0 : 0;
+    const __nv_bfloat16 *src = (is_k ? k : q) + r * kHeadDim;
+    __nv_bfloat16 *dst = (is_k ? kn : qn) + r * kHeadDim;
+    float x[16];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const uint2 w = __ldg(reinterpret_cast<const uint2 *>(src) + lane8 + 8 * m);
+        x[4 * m + 0] = bf16_lo(w.x); x[4 * m + 1] = bf16_hi(w.x);
+        x[4 * m + 2] = bf16_lo(w.y); x[4 * m + 3] = bf16_hi(w.y);
+    }
+    l2norm_8lanes(x);
+    if (!live) return;
+#pragma unroll
+    for (int m = 0; m < 4; ++m)
+        reinterpret_cast<uint2 *>(dst)[lane8 + 8 * m] =
+            make_uint2(pack_bf16x2(x[4 * m], x[4 * m + 1]), pack_bf16x2(x[4 * m + 2], x[4 * m + 3]));
+}
+
+cudaError_t launch_qk_l2norm(const void *q, const void *k, int64_t rows, void *qn, void *kn,
+                             cudaStream_t stream) {
+    if (rows <= 0) return cudaSuccess;
+    const int64_t threads = 2 * rows * 8;
+    const int64_t blocks = (threads + 255) / 256;
+    if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+    qk_l2norm_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16 *>(q), static_cast<const __nv_bfloat16 *>(k), rows,
+        static_cast<__nv_bfloat16 *>(qn), static_cast<__nv_bfloat16 *>(kn));
     return cudaGetLastError();
 }
 

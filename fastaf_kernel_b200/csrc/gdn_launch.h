@@ -18,6 +18,7 @@ struct DecodeArgs {
     int gate_dtype, param_dtype;
     void *out;                   // bf16 [B, Hv, D]
     float *new_state;            // may equal state
+    int qk_l2norm;               // 1: q, k <- bf16(x / sqrt(sum x^2 + 1e-6)) inside the kernel
 };
 
 struct PrefillArgs {
@@ -37,6 +38,10 @@ struct PrefillArgs {
 void set_last_error(const char *msg);
 
 cudaError_t launch_decode(const DecodeArgs &p, cudaStream_t stream);
+// qn, kn <- bf16(x / sqrt(sum x^2 + 1e-6)) for every 128-element head vector of q, k
+// ([rows][128] bf16, rows = tokens * heads); the same arithmetic as the decode kernel's.
+cudaError_t launch_qk_l2norm(const void *q, const void *k, int64_t rows, void *qn, void *kn,
+                             cudaStream_t stream);
 cudaError_t launch_prefill_recurrent(const PrefillArgs &p, cudaStream_t stream);
 cudaError_t launch_prefill_chunked(const PrefillArgs &p, cudaStream_t stream);
 bool prefill_chunked_supported(const PrefillArgs &p);

@@ -43,6 +43,9 @@ extern "C" {
 #define GDN_DTYPE_F32 0
 #define GDN_DTYPE_BF16 1
 
+/* Option bits for gdn_prefill_flags() / gdn_decode_flags(). */
+#define GDN_FLAG_QK_L2NORM 1   /* L2-normalise every q and k head vector first (see below) */
+
 /* Prefill kernel choice for gdn_prefill_ex(). */
 #define GDN_PREFILL_AUTO 0      /* TCGEN05 from 2048 packed tokens, else CHUNKED, else RECURRENT */
 #define GDN_PREFILL_CHUNKED 1   /* chunked (C=64) WY/UT kernel on the tensor cores (mma.sync) */
@@ -89,6 +92,23 @@ GDN_API int gdn_prefill_ex(const void *q, const void *k, const void *v, const fl
                    int num_qk_heads, int num_v_heads, int head_size, float scale,
                    int gate_dtype, int param_dtype, void *output, float *new_state,
                    int method, void *stream);
+
+/*
+ * gdn_prefill_ex with option bits.  GDN_FLAG_QK_L2NORM replaces every 128-element head
+ * vector x of q and k by bf16(x / sqrt(sum(x^2) + 1e-6)), computed in fp32 from the
+ * bf16 inputs -- the L2 normalisation Gated DeltaNet layers apply before the
+ * recurrence, rounded to bf16 as a normalisation layer would emit it -- before the
+ * prefill runs (a pre-pass into scratch from the library's memory pool, since the
+ * tensor-core kernels read q and k straight into their operand tiles).  The reference
+ * never normalises (its benchmark inputs arrive normalised), so gdn_prefill and
+ * gdn_prefill_ex run with no flags.  No counterpart in the reference.
+ */
+GDN_API int gdn_prefill_flags(const void *q, const void *k, const void *v, const float *state,
+                      const void *A_log, const void *a, const void *dt_bias, const void *b,
+                      const int32_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
+                      int num_qk_heads, int num_v_heads, int head_size, float scale,
+                      int gate_dtype, int param_dtype, void *output, float *new_state,
+                      int method, int flags, void *stream);
 
 /*
  * gdn_prefill_ex with a caller-provided workspace (no allocation inside the call).
@@ -163,6 +183,16 @@ GDN_API int gdn_decode(const void *q, const void *k, const void *v, const float 
                int64_t batch, int num_qk_heads, int num_v_heads, int head_size,
                float scale, int gate_dtype, int param_dtype, void *output,
                float *new_state, void *stream);
+
+/* gdn_decode with option bits.  GDN_FLAG_QK_L2NORM: q and k are L2-normalised inside
+ * the decode kernel, with the same arithmetic as gdn_prefill_flags (so a normalised
+ * prefill followed by normalised decode steps continues the same recurrence).  No
+ * counterpart in the reference. */
+GDN_API int gdn_decode_flags(const void *q, const void *k, const void *v, const float *state,
+                     const void *A_log, const void *a, const void *dt_bias, const void *b,
+                     int64_t batch, int num_qk_heads, int num_v_heads, int head_size,
+                     float scale, int gate_dtype, int param_dtype, void *output,
+                     float *new_state, int flags, void *stream);
 
 /*
  * Synchronizes `stream` and reports whether any chunked-prefill kernel since the

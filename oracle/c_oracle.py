@@ -39,10 +39,10 @@ def _load():
         vp, i64, i32, f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
         lib.gdn_oracle_prefill.restype = i32
         lib.gdn_oracle_prefill.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64,
-                                           i32, i32, i32, f32, i32, i32, vp, vp, i32]
+                                           i32, i32, i32, f32, i32, i32, vp, vp, i32, i32]
         lib.gdn_oracle_decode.restype = i32
         lib.gdn_oracle_decode.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i64, i32, i32,
-                                          i32, f32, i32, i32, vp, vp, i32]
+                                          i32, f32, i32, i32, vp, vp, i32, i32]
         _lib = lib
     return _lib
 
@@ -63,8 +63,10 @@ def _threads(num_threads: Optional[int]) -> int:
 
 
 def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale,
-            num_threads: Optional[int] = None) -> Tuple[torch.Tensor, torch.Tensor]:
-    """Varlen prefill on the CPU; returns (output bf16 [T,Hv,D], new_state fp32 [N,Hv,D,D])."""
+            num_threads: Optional[int] = None,
+            qk_l2norm: bool = False) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Varlen prefill on the CPU; returns (output bf16 [T,Hv,D], new_state fp32 [N,Hv,D,D]).
+    ``qk_l2norm`` applies the library's optional q/k L2 normalisation first."""
     lib = _load()
     q = _cpu(q, torch.bfloat16); k = _cpu(k, torch.bfloat16); v = _cpu(v, torch.bfloat16)
     if k.shape[1] != q.shape[1]:
@@ -85,7 +87,7 @@ def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale,
     rc = lib.gdn_oracle_prefill(_ptr(q), _ptr(k), _ptr(v), _ptr(st), _ptr(A_log), _ptr(a),
                                 _ptr(dt_bias), _ptr(b), _ptr(cu), N, T, Hq, Hv, D, float(scale),
                                 _DTYPE_CODE[gdt], _DTYPE_CODE[pdt], _ptr(out), _ptr(ns),
-                                _threads(num_threads))
+                                _threads(num_threads), int(qk_l2norm))
     if rc != 0:
         raise ValueError(f"gdn_oracle_prefill rejected its arguments (rc={rc})")
     return out, ns
@@ -93,7 +95,7 @@ def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale,
 
 def decode(q, k, v, state, A_log, a, dt_bias, b, scale,
            num_threads: Optional[int] = None,
-           inplace: bool = False) -> Tuple[torch.Tensor, torch.Tensor]:
+           inplace: bool = False, qk_l2norm: bool = False) -> Tuple[torch.Tensor, torch.Tensor]:
     """Single-token decode on the CPU.  q,k [B,1,Hq,D], v [B,1,Hv,D], a,b [B,1,Hv].
 
     With ``inplace=True`` and an fp32 contiguous CPU ``state`` the update is
@@ -123,7 +125,7 @@ def decode(q, k, v, state, A_log, a, dt_bias, b, scale,
     rc = lib.gdn_oracle_decode(_ptr(q), _ptr(k), _ptr(v), _ptr(st), _ptr(A_log), _ptr(a),
                                _ptr(dt_bias), _ptr(b), B, Hq, Hv, D, float(scale),
                                _DTYPE_CODE[gdt], _DTYPE_CODE[pdt], _ptr(out), _ptr(ns),
-                               _threads(num_threads))
+                               _threads(num_threads), int(qk_l2norm))
     if rc != 0:
         raise ValueError(f"gdn_oracle_decode rejected its arguments (rc={rc})")
     return out.unsqueeze(1), ns

@@ -23,6 +23,11 @@
  * torch's BLAS summation order in the last bits.
  *
  * Chains are independent, so they run in parallel under OpenMP.
+ *
+ * qk_l2norm != 0 first replaces every q and k head vector x by
+ * bf16(x / sqrt(sum x^2 + 1e-6)) (fp32 arithmetic) -- the library's optional L2
+ * normalisation, which the reference does not have; with qk_l2norm == 0 the
+ * functions follow the reference exactly.
  */
 #include <math.h>
 #include <stdint.h>
@@ -62,6 +67,11 @@ static inline float dot8(const float *x, const float *y, int n) {
     return ((p[0] + p[1]) + (p[2] + p[3])) + ((p[4] + p[5]) + (p[6] + p[7]));
 }
 
+static void l2norm_bf16(float *x, int n) {
+    const float inv = 1.0f / sqrtf(dot8(x, x, n) + 1e-6f);
+    for (int i = 0; i < n; ++i) x[i] = bf16_to_f32(f32_to_bf16(x[i] * inv));
+}
+
 /*
  * q, k: bf16 [T, Hq, D]; v: bf16 [T, Hv, D]; a, b: [T, Hv] (gate_dtype);
  * A_log, dt_bias: [Hv] (param_dtype); state: fp32 [N, Hv, D, D] or NULL;
@@ -73,7 +83,7 @@ int gdn_oracle_prefill(const uint16_t *q, const uint16_t *k, const uint16_t *v,
                        const void *dt_bias, const void *b, const int32_t *cu_seqlens,
                        int64_t N, int64_t T, int Hq, int Hv, int D, float scale,
                        int gate_dtype, int param_dtype, uint16_t *out,
-                       float *new_state, int num_threads) {
+                       float *new_state, int num_threads, int qk_l2norm) {
     if (Hq <= 0 || Hv <= 0 || D <= 0 || D > 1024 || Hv % Hq != 0 || N < 0 || T < 0) return -1;
     if (scale == 0.0f) scale = 1.0f / sqrtf((float)D);
     const int ratio = Hv / Hq;
@@ -102,6 +112,7 @@ int gdn_oracle_prefill(const uint16_t *q, const uint16_t *k, const uint16_t *v,
                     const uint16_t *vp = v + ((size_t)t * Hv + h) * D;
                     uint16_t *op = out + ((size_t)t * Hv + h) * D;
                     for (int i = 0; i < D; ++i) { kf[i] = bf16_to_f32(kp[i]); qf[i] = bf16_to_f32(qp[i]); }
+                    if (qk_l2norm) { l2norm_bf16(kf, D); l2norm_bf16(qf, D); }
                     for (int r = 0; r < D; ++r) {
                         float *row = S + (size_t)r * D;
                         for (int i = 0; i < D; ++i) row[i] *= g;
@@ -122,7 +133,7 @@ int gdn_oracle_decode(const uint16_t *q, const uint16_t *k, const uint16_t *v,
                       const float *state, const void *A_log, const void *a,
                       const void *dt_bias, const void *b, int64_t B, int Hq, int Hv,
                       int D, float scale, int gate_dtype, int param_dtype,
-                      uint16_t *out, float *new_state, int num_threads) {
+                      uint16_t *out, float *new_state, int num_threads, int qk_l2norm) {
     if (Hq <= 0 || Hv <= 0 || D <= 0 || D > 1024 || Hv % Hq != 0 || B < 0) return -1;
     if (scale == 0.0f) scale = 1.0f / sqrtf((float)D);
     const int ratio = Hv / Hq;
@@ -149,6 +160,7 @@ int gdn_oracle_decode(const uint16_t *q, const uint16_t *k, const uint16_t *v,
         const uint16_t *vp = v + ((size_t)n * Hv + h) * D;
         uint16_t *op = out + ((size_t)n * Hv + h) * D;
         for (int i = 0; i < D; ++i) { kf[i] = bf16_to_f32(kp[i]); qf[i] = bf16_to_f32(qp[i]); }
+        if (qk_l2norm) { l2norm_bf16(kf, D); l2norm_bf16(qf, D); }
         for (int r = 0; r < D; ++r) {
             float *row = S + (size_t)r * D;
             for (int i = 0; i < D; ++i) row[i] *= g;
