@@ -428,7 +428,9 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                 // tile (two threads per 4-byte word, conflict-free) and writes row k.
                 const uint8_t *src = sm + OFF_KQ + st * KQ_STAGE + 8192 + (pt >> 6) * 16384 + (pt & 7) * 2;
                 const int kc = (pt & 63) >> 3;
-#pragma unroll
+                // (rolled: these warps' code shares the instruction caches with the other
+                // roles, and keeping it small measurably shortens the whole chain)
+#pragma unroll 1
                 for (int ch = 0; ch < 8; ++ch) {
                     uint32_t w[4];
 #pragma unroll
@@ -454,7 +456,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             warp_arrive(b_qs, lane);
             // -W as bf16 hi/lo, MN-major [k][i] (TMEM lane k holds row k of W^T)
             if (!wait_warp(b_wdone, c & 1, kWaitWU, abort)) break;
-#pragma unroll
+#pragma unroll 1
             for (int hf = 0; hf < 2; ++hf) {
                 uint32_t r[32];
                 tmem_ld32(tmem_addr(tm, lane_base, TM_W + 32 * hf), r);
