@@ -17,7 +17,10 @@
 namespace {
 
 thread_local char g_last_error[512] = "";
-constexpr int64_t kAutoTcMinTokens = 2048;
+// From 256 packed tokens the tcgen05 pipeline beats the single-launch mma.sync kernel
+// on B200 (256 tokens 43 vs 51 us, 1024 tokens 56 vs 84 us at Hq 16 / Hv 32); below it
+// the extra prep launch does not pay off (64-128 tokens: 42 vs 32 us).
+constexpr int64_t kAutoTcMinTokens = 256;
 
 int fail(int code, const char *fmt, ...) {
     va_list ap;
@@ -201,7 +204,7 @@ static int prefill_impl(const void *q, const void *k, const void *v, const float
         if (rc2 != GDN_OK) return rc2;
         return cuda_status(ef, "gdn_prefill (qk l2norm) scratch release");
     }
-    // auto: the tcgen05 pipeline for large batches; below ~2K tokens its extra prep
+    // auto: the tcgen05 pipeline from kAutoTcMinTokens tokens; below that its extra prep
     // launch does not pay off and the single-launch mma.sync kernel is faster.
     if (method == GDN_PREFILL_AUTO && gdn_prefill_resolve(total_tokens, method) == GDN_PREFILL_TCGEN05)
         method = GDN_PREFILL_TCGEN05;

@@ -47,7 +47,7 @@ extern "C" {
 #define GDN_FLAG_QK_L2NORM 1   /* L2-normalise every q and k head vector first (see below) */
 
 /* Prefill kernel choice for gdn_prefill_ex(). */
-#define GDN_PREFILL_AUTO 0      /* TCGEN05 from 2048 packed tokens, else CHUNKED, else RECURRENT */
+#define GDN_PREFILL_AUTO 0      /* TCGEN05 from 256 packed tokens, else CHUNKED, else RECURRENT */
 #define GDN_PREFILL_CHUNKED 1   /* chunked (C=64) WY/UT kernel on the tensor cores (mma.sync) */
 #define GDN_PREFILL_RECURRENT 2 /* token-serial CUDA-core kernel */
 #define GDN_PREFILL_TCGEN05 3   /* chunked (C=64) kernel on tcgen05 + TMEM + TMA; T >= 64 */

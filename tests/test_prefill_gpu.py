@@ -181,10 +181,10 @@ def test_prefill_output_destination_passing():
 
 
 def test_auto_method_resolution():
-    """auto runs the tcgen05 pipeline from 2048 packed tokens, the mma.sync kernel below."""
-    assert fk.prefill_method(2048) == "tcgen05"
+    """auto runs the tcgen05 pipeline from 256 packed tokens, the mma.sync kernel below."""
+    assert fk.prefill_method(256) == "tcgen05"
     assert fk.prefill_method(131072) == "tcgen05"
-    assert fk.prefill_method(2047) == "chunked"
+    assert fk.prefill_method(255) == "chunked"
     assert fk.prefill_method(1) == "chunked"
     assert fk.prefill_method(5000, "recurrent") == "recurrent"
 
