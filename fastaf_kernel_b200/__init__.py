@@ -6,6 +6,6 @@ Drop-in for the reference's ``kernel`` / ``kernel_decode`` entry points
 """
 
 from .api import (device_status, kernel, kernel_decode, kernel_dps, kernel_decode_dps,  # noqa: F401
-                  prefill_method)
+                  output_gate, prefill_method)
 
 __version__ = "0.1.0"

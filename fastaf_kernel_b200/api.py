@@ -17,7 +17,11 @@ unchanged:
   * ``use_qk_l2norm=True`` L2-normalises every q and k head vector first,
     x <- bf16(x / sqrt(sum x^2 + 1e-6)) in fp32 -- the normalisation Gated DeltaNet
     layers apply before the recurrence (fused into the decode kernel; a pre-pass for
-    prefill).  Off by default: the reference never normalises.
+    prefill).  Off by default: the reference never normalises;
+  * ``output_gate=z, norm_weight=w`` (optionally ``norm_eps=``) apply the gated
+    RMSNorm of Gated DeltaNet layers to the output,
+    o <- o / sqrt(mean(o^2) + eps) * w * silu(z) per head vector (``output_gate``
+    below); the reference returns o itself.
 """
 
 from __future__ import annotations
@@ -30,7 +34,7 @@ import torch
 from . import _lib
 
 __all__ = ["kernel", "kernel_decode", "kernel_dps", "kernel_decode_dps", "device_status",
-           "prefill_method"]
+           "prefill_method", "output_gate"]
 
 _GATE_DTYPES = {torch.float32: _lib.GDN_DTYPE_F32, torch.bfloat16: _lib.GDN_DTYPE_BF16}
 _METHODS = {"auto": _lib.GDN_PREFILL_AUTO, "chunked": _lib.GDN_PREFILL_CHUNKED,
@@ -95,7 +99,9 @@ def kernel(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: Optional[to
            cu_seqlens: torch.Tensor, scale: Optional[float], *,
            output: Optional[torch.Tensor] = None, new_state: Optional[torch.Tensor] = None,
            method: str = "auto", validate: bool = True,
-           use_qk_l2norm: bool = False) -> Tuple[torch.Tensor, torch.Tensor]:
+           use_qk_l2norm: bool = False, output_gate: Optional[torch.Tensor] = None,
+           norm_weight: Optional[torch.Tensor] = None,
+           norm_eps: float = 1e-6) -> Tuple[torch.Tensor, torch.Tensor]:
     """Varlen Gated DeltaNet prefill (solution/triton/kernel.py:416-489).
 
     q, k [T, Hq, D] bf16; v [T, Hv, D] bf16; state [N, Hv, D, D] fp32 k-last or
@@ -164,6 +170,8 @@ def kernel(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: Optional[to
             _ptr(b), _ptr(cu), N, T, Hq, Hv, D, scale, _GATE_DTYPES[a.dtype],
             _GATE_DTYPES[A_log.dtype], _ptr(output), _ptr(new_state), _METHODS[method],
             _lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm else 0, stream))
+    if output_gate is not None or norm_weight is not None:
+        _gated_rmsnorm(output, output_gate, norm_weight, norm_eps)
     return output, new_state
 
 
@@ -172,7 +180,9 @@ def kernel_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                   dt_bias: torch.Tensor, b: torch.Tensor, scale: Optional[float], *,
                   output: Optional[torch.Tensor] = None,
                   new_state: Optional[torch.Tensor] = None,
-                  use_qk_l2norm: bool = False) -> Tuple[torch.Tensor, torch.Tensor]:
+                  use_qk_l2norm: bool = False, output_gate: Optional[torch.Tensor] = None,
+                  norm_weight: Optional[torch.Tensor] = None,
+                  norm_eps: float = 1e-6) -> Tuple[torch.Tensor, torch.Tensor]:
     """Single-token Gated DeltaNet decode (solution/triton/kernel.py:492-556).
 
     q, k [B, 1, Hq, D] bf16; v [B, 1, Hv, D] bf16; a, b [B, 1, Hv];
@@ -232,7 +242,44 @@ def kernel_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
             _ptr(b), B, Hq, Hv, D, scale, _GATE_DTYPES[a.dtype], _GATE_DTYPES[A_log.dtype],
             _ptr(output), _ptr(new_state), _lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm else 0,
             stream))
+    if output_gate is not None or norm_weight is not None:
+        _gated_rmsnorm(output, output_gate, norm_weight, norm_eps)
     return output, new_state
+
+
+def output_gate(output: torch.Tensor, gate: torch.Tensor, weight: torch.Tensor,
+                eps: float = 1e-6) -> torch.Tensor:
+    """In place: output <- output / sqrt(mean(output^2) + eps) * weight * silu(gate) over
+    every 128-element head vector (the gated RMSNorm Gated DeltaNet layers apply before
+    the output projection).  output, gate: bf16 of the same shape [..., D] on one CUDA
+    device; weight [D] fp32 or bf16.  Returns ``output``."""
+    return _gated_rmsnorm(output, gate, weight, eps)
+
+
+def _gated_rmsnorm(output, gate, weight, eps):
+    if gate is None or weight is None:
+        raise ValueError("output gating needs both a gate and a norm weight")
+    if not eps >= 0.0:
+        raise ValueError("eps must be >= 0")
+    device = output.device
+    _require_cuda("output", output, device)
+    _require_cuda("gate", gate, device)
+    _require_cuda("weight", weight, device)
+    if output.dtype != torch.bfloat16 or not output.is_contiguous():
+        raise ValueError("output must be a contiguous bf16 tensor")
+    if tuple(gate.shape) != tuple(output.shape):
+        raise ValueError(f"gate shape {tuple(gate.shape)} must equal output shape {tuple(output.shape)}")
+    D = output.shape[-1]
+    if weight.numel() != D:
+        raise ValueError(f"weight must have {D} elements")
+    gate = _bf16("gate", gate)
+    weight = _gate(weight)
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        _lib.check(lib.gdn_output_gate(_ptr(output), _ptr(gate), _ptr(weight), _GATE_DTYPES[weight.dtype],
+                                       output.numel() // D, D, float(eps), stream))
+    return output
 
 
 def kernel_dps(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state):

@@ -22,7 +22,7 @@ SELFTEST_LIB_PATH = os.path.join(LIB_DIR, "libgdn_b200_selftest.so")
 INCLUDE = os.path.join(REPO_DIR, "include")
 
 SOURCES = ["gdn_api.cu", "gdn_decode.cu", "gdn_prefill_recurrent.cu", "gdn_prefill_chunked.cu",
-           "gdn_chunk_prep.cu", "gdn_prefill_tc.cu", "gdn_prefill_noalloc.cu"]
+           "gdn_chunk_prep.cu", "gdn_prefill_tc.cu", "gdn_prefill_noalloc.cu", "gdn_output_gate.cu"]
 # Known-answer checks of the tcgen05/TMA primitives, a separate test library.
 SELFTEST_SOURCES = ["gdn_selftest.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -268,6 +268,23 @@ int gdn_prefill_ws(const void *q, const void *k, const void *v, const float *sta
                         new_state, method, workspace, workspace_bytes, stream);
 }
 
+int gdn_output_gate(void *output, const void *gate, const void *weight, int weight_dtype, int64_t num_vectors,
+                    int head_size, float eps, void *stream) {
+    g_last_error[0] = '\0';
+    if (head_size != 128) return fail(GDN_ERR_UNSUPPORTED, "head_size=%d (only 128 is built)", head_size);
+    if (num_vectors < 0) return fail(GDN_ERR_INVALID_ARGUMENT, "num_vectors=%lld < 0", (long long)num_vectors);
+    if (weight_dtype != GDN_DTYPE_F32 && weight_dtype != GDN_DTYPE_BF16)
+        return fail(GDN_ERR_INVALID_ARGUMENT, "unknown weight_dtype %d", weight_dtype);
+    if (!(eps >= 0.0f)) return fail(GDN_ERR_INVALID_ARGUMENT, "eps must be >= 0");
+    if (num_vectors == 0) return GDN_OK;
+    if (!output || !gate || !weight) return fail(GDN_ERR_INVALID_ARGUMENT, "null output, gate or weight");
+    if (!aligned16(output) || !aligned16(gate))
+        return fail(GDN_ERR_INVALID_ARGUMENT, "output and gate must be 16-byte aligned");
+    return cuda_status(gdn::launch_output_gate(output, gate, weight, weight_dtype, num_vectors, eps,
+                                               static_cast<cudaStream_t>(stream)),
+                       "gdn_output_gate launch");
+}
+
 int gdn_prefill_resolve(int64_t total_tokens, int method) {
     gdn::PrefillArgs p{};
     p.total_tokens = total_tokens;

@@ -38,6 +38,9 @@ struct PrefillArgs {
 void set_last_error(const char *msg);
 
 cudaError_t launch_decode(const DecodeArgs &p, cudaStream_t stream);
+// o <- bf16(o / sqrt(mean(o^2) + eps) * w * silu(z)) per 128-element vector, in place.
+cudaError_t launch_output_gate(void *o, const void *z, const void *w, int w_dtype, int64_t vectors, float eps,
+                               cudaStream_t stream);
 // qn, kn <- bf16(x / sqrt(sum x^2 + 1e-6)) for every 128-element head vector of q, k
 // ([rows][128] bf16, rows = tokens * heads); the same arithmetic as the decode kernel's.
 cudaError_t launch_qk_l2norm(const void *q, const void *k, int64_t rows, void *qn, void *kn,

@@ -151,6 +151,22 @@ GDN_API int gdn_prefill_noalloc(const void *q, const void *k, const void *v, con
                         int gate_dtype, int param_dtype, void *output, float *new_state,
                         void *stream);
 
+/*
+ * Gated RMSNorm of the recurrence output, in place:
+ *   output <- bf16(output / sqrt(mean(output^2) + eps) * weight * silu(gate))
+ * over every 128-element head vector (num_vectors = tokens * v-heads), in fp32 from
+ * the bf16 output and gate.  Gated DeltaNet layers apply it between the recurrence
+ * and the output projection; call it on the output of gdn_prefill* / gdn_decode* on
+ * the same stream.
+ *   output   bf16 [num_vectors, head_size], 16-byte aligned (read and written)
+ *   gate     bf16 [num_vectors, head_size], 16-byte aligned
+ *   weight   [head_size] (weight_dtype: GDN_DTYPE_F32 or GDN_DTYPE_BF16)
+ * Requirements: head_size == 128.  No counterpart in the reference (its entry points
+ * return the ungated output).
+ */
+GDN_API int gdn_output_gate(void *output, const void *gate, const void *weight, int weight_dtype,
+                    int64_t num_vectors, int head_size, float eps, void *stream);
+
 /* The prefill kernel (GDN_PREFILL_*) a call with `method` runs for `total_tokens` packed
  * tokens on the current device: AUTO resolves to TCGEN05, CHUNKED or RECURRENT; other
  * values are returned unchanged.  No counterpart in the reference. */

@@ -1,0 +1,74 @@
+"""Gated RMSNorm of the recurrence output (``output_gate=``, ``norm_weight=``):
+o <- o / sqrt(mean(o^2) + eps) * w * silu(z) per 128-element head vector.  The
+reference returns the ungated o; Gated DeltaNet layers apply this step before the
+output projection.  Checked against a plain PyTorch fp32 restatement."""
+import pytest
+import torch
+
+import fastaf_kernel_b200 as fk
+from fastaf_kernel_b200 import workloads as W
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+def _reference(o, z, w, eps):
+    x = o.float()
+    y = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w.float() * torch.nn.functional.silu(z.float())
+    return y.to(torch.bfloat16)
+
+
+def _assert_close(got, ref):
+    # bf16 outputs: one bf16 rounding step apart at most
+    diff = (got.float() - ref.float()).abs()
+    tol = 1e-2 * ref.float().abs() + 1e-3
+    assert bool((diff <= tol).all()), f"max excess {(diff - tol).max().item():.3e}"
+
+
+@pytest.mark.parametrize("shape,wdtype", [((7, 32, 128), torch.float32), ((1000, 8, 128), torch.bfloat16),
+                                          ((3, 1, 128), torch.float32)])
+def test_output_gate_matches_torch(shape, wdtype):
+    g = torch.Generator(device=DEV).manual_seed(5)
+    o = (torch.randn(shape, generator=g, device=DEV) * 0.3).to(torch.bfloat16)
+    z = torch.randn(shape, generator=g, device=DEV).to(torch.bfloat16)
+    w = (torch.rand(128, generator=g, device=DEV) + 0.5).to(wdtype)
+    ref = _reference(o, z, w, 1e-6)
+    got = fk.output_gate(o.clone(), z, w, 1e-6)
+    torch.cuda.synchronize()
+    _assert_close(got, ref)
+
+
+@pytest.mark.parametrize("method", ["tcgen05", "chunked", "recurrent"])
+def test_prefill_with_output_gate(method):
+    x = W.prefill_inputs([300, 77, 64], seed=71, Hq=4, Hv=8, device=DEV)
+    T = x["q"].shape[0]
+    g = torch.Generator(device=DEV).manual_seed(6)
+    z = torch.randn((T, 8, 128), generator=g, device=DEV).to(torch.bfloat16)
+    w = torch.rand(128, generator=g, device=DEV) + 0.5
+    args = (x["q"], x["k"], x["v"], x["state"], x["A_log"], x["a"], x["dt_bias"], x["b"], x["cu_seqlens"], x["scale"])
+    o_plain, s_plain = fk.kernel(*args, method=method)
+    o_gated, s_gated = fk.kernel(*args, method=method, output_gate=z, norm_weight=w, norm_eps=1e-5)
+    fk.device_status()
+    assert torch.equal(s_gated, s_plain)
+    _assert_close(o_gated, _reference(o_plain, z, w, 1e-5))
+
+
+def test_decode_with_output_gate():
+    d = W.decode_inputs(16, seed=72, Hq=4, Hv=8, device=DEV)
+    g = torch.Generator(device=DEV).manual_seed(7)
+    z = torch.randn((16, 1, 8, 128), generator=g, device=DEV).to(torch.bfloat16)
+    w = (torch.rand(128, generator=g, device=DEV) + 0.5).to(torch.bfloat16)
+    args = (d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"], d["dt_bias"], d["b"], d["scale"])
+    o_plain, s_plain = fk.kernel_decode(*args)
+    o_gated, s_gated = fk.kernel_decode(*args, output_gate=z, norm_weight=w)
+    fk.device_status()
+    assert torch.equal(s_gated, s_plain)
+    _assert_close(o_gated, _reference(o_plain, z, w, 1e-6))
+
+
+def test_output_gate_rejects_bad_arguments():
+    o = torch.zeros((4, 2, 128), dtype=torch.bfloat16, device=DEV)
+    with pytest.raises(ValueError):
+        fk.output_gate(o, torch.zeros((4, 2, 64), dtype=torch.bfloat16, device=DEV), torch.ones(128, device=DEV))
+    with pytest.raises(ValueError):
+        fk.output_gate(o, torch.zeros_like(o), torch.ones(64, device=DEV))
