@@ -165,13 +165,19 @@ def kernel(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: Optional[to
     lib = _lib.load()
     with torch.cuda.device(device):
         stream = torch.cuda.current_stream(device).cuda_stream
-        _lib.check(lib.gdn_prefill_flags(
-            _ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias),
-            _ptr(b), _ptr(cu), N, T, Hq, Hv, D, scale, _GATE_DTYPES[a.dtype],
-            _GATE_DTYPES[A_log.dtype], _ptr(output), _ptr(new_state), _METHODS[method],
-            _lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm else 0, stream))
-    if output_gate is not None or norm_weight is not None:
-        _gated_rmsnorm(output, output_gate, norm_weight, norm_eps)
+        flags = _lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm else 0
+        if output_gate is None and norm_weight is None:
+            _lib.check(lib.gdn_prefill_flags(
+                _ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias),
+                _ptr(b), _ptr(cu), N, T, Hq, Hv, D, scale, _GATE_DTYPES[a.dtype],
+                _GATE_DTYPES[A_log.dtype], _ptr(output), _ptr(new_state), _METHODS[method], flags, stream))
+        else:
+            z, w = _check_output_gate(output, output_gate, norm_weight, norm_eps)
+            _lib.check(lib.gdn_prefill_gated(
+                _ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias),
+                _ptr(b), _ptr(cu), N, T, Hq, Hv, D, scale, _GATE_DTYPES[a.dtype],
+                _GATE_DTYPES[A_log.dtype], _ptr(output), _ptr(new_state), _ptr(z), _ptr(w),
+                _GATE_DTYPES[w.dtype], float(norm_eps), _METHODS[method], flags, stream))
     return output, new_state
 
 
@@ -256,7 +262,8 @@ def output_gate(output: torch.Tensor, gate: torch.Tensor, weight: torch.Tensor,
     return _gated_rmsnorm(output, gate, weight, eps)
 
 
-def _gated_rmsnorm(output, gate, weight, eps):
+def _check_output_gate(output, gate, weight, eps):
+    """Validated (gate bf16 contiguous, weight fp32/bf16 contiguous) for gating ``output``."""
     if gate is None or weight is None:
         raise ValueError("output gating needs both a gate and a norm weight")
     if not eps >= 0.0:
@@ -272,8 +279,13 @@ def _gated_rmsnorm(output, gate, weight, eps):
     D = output.shape[-1]
     if weight.numel() != D:
         raise ValueError(f"weight must have {D} elements")
-    gate = _bf16("gate", gate)
-    weight = _gate(weight)
+    return _bf16("gate", gate), _gate(weight)
+
+
+def _gated_rmsnorm(output, gate, weight, eps):
+    gate, weight = _check_output_gate(output, gate, weight, eps)
+    device = output.device
+    D = output.shape[-1]
     lib = _lib.load()
     with torch.cuda.device(device):
         stream = torch.cuda.current_stream(device).cuda_stream

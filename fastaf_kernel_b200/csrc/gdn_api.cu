@@ -149,13 +149,24 @@ int gdn_decode_flags(const void *q, const void *k, const void *v, const float *s
     return cuda_status(gdn::launch_decode(p, static_cast<cudaStream_t>(stream)), "gdn_decode launch");
 }
 
+// The optional gated RMSNorm of the output, as its own pass after the prefill (a
+// version fused into the tcgen05 chains' output store that loaded the gate rows there
+// measured 2x slower: those warps feed the next chunk's delta batch).
+static int gate_output(const gdn::PrefillArgs &p, cudaStream_t s) {
+    if (!p.out_gate) return GDN_OK;
+    return cuda_status(gdn::launch_output_gate(p.out, p.out_gate, p.norm_w, p.norm_w_dtype,
+                                               p.total_tokens * p.Hv, p.norm_eps, s),
+                       "gdn_prefill output gate launch");
+}
+
 static int prefill_impl(const void *q, const void *k, const void *v, const float *state,
                         const void *A_log, const void *a, const void *dt_bias, const void *b,
                         const int32_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
                         int num_qk_heads, int num_v_heads, int head_size, float scale,
                         int gate_dtype, int param_dtype, void *output, float *new_state,
                         int method, void *workspace, size_t workspace_bytes, void *stream,
-                        int flags = 0) {
+                        int flags = 0, const void *out_gate = nullptr, const void *norm_w = nullptr,
+                        int norm_w_dtype = 0, float norm_eps = 0.0f) {
     g_last_error[0] = '\0';
     if (flags & ~GDN_FLAG_QK_L2NORM) return fail(GDN_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
     int rc = check_common(num_qk_heads, num_v_heads, head_size, gate_dtype, param_dtype, q, k, v,
@@ -182,6 +193,10 @@ static int prefill_impl(const void *q, const void *k, const void *v, const float
                        num_qk_heads, num_v_heads,
                        scale == 0.0f ? 1.0f / sqrtf(static_cast<float>(head_size)) : scale,
                        gate_dtype, param_dtype, output, new_state};
+    p.out_gate = out_gate;
+    p.norm_w = norm_w;
+    p.norm_w_dtype = norm_w_dtype;
+    p.norm_eps = norm_eps;
     const auto s = static_cast<cudaStream_t>(stream);
     if (flags & GDN_FLAG_QK_L2NORM) {
         // Normalised q and k into pool scratch, then the prefill on them.
@@ -189,7 +204,8 @@ static int prefill_impl(const void *q, const void *k, const void *v, const float
         if (qk_bytes == 0)
             return prefill_impl(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs, total_tokens,
                                 num_qk_heads, num_v_heads, head_size, scale, gate_dtype, param_dtype, output,
-                                new_state, method, workspace, workspace_bytes, stream, 0);
+                                new_state, method, workspace, workspace_bytes, stream, 0, out_gate, norm_w,
+                                norm_w_dtype, norm_eps);
         void *qk = nullptr;
         cudaError_t e = pool_alloc(&qk, 2 * qk_bytes, s);
         if (e != cudaSuccess) return cuda_status(e, "gdn_prefill (qk l2norm) scratch");
@@ -199,7 +215,8 @@ static int prefill_impl(const void *q, const void *k, const void *v, const float
                                    : prefill_impl(qn, kn, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs,
                                                   total_tokens, num_qk_heads, num_v_heads, head_size, scale,
                                                   gate_dtype, param_dtype, output, new_state, method, workspace,
-                                                  workspace_bytes, stream, 0);
+                                                  workspace_bytes, stream, 0, out_gate, norm_w, norm_w_dtype,
+                                                  norm_eps);
         const cudaError_t ef = cudaFreeAsync(qk, s);
         if (rc2 != GDN_OK) return rc2;
         return cuda_status(ef, "gdn_prefill (qk l2norm) scratch release");
@@ -217,7 +234,9 @@ static int prefill_impl(const void *q, const void *k, const void *v, const float
             if (workspace_bytes < need)
                 return fail(GDN_ERR_INVALID_ARGUMENT, "workspace of %zu bytes is smaller than the %zu needed",
                             workspace_bytes, need);
-            return cuda_status(gdn::launch_prefill_tc(p, workspace, s), "gdn_prefill (tcgen05) launch");
+            const cudaError_t e = gdn::launch_prefill_tc(p, workspace, s);
+            if (e != cudaSuccess) return cuda_status(e, "gdn_prefill (tcgen05) launch");
+            return gate_output(p, s);
         }
         void *ws = nullptr;
         cudaError_t e = pool_alloc(&ws, need, s);
@@ -225,14 +244,16 @@ static int prefill_impl(const void *q, const void *k, const void *v, const float
         e = gdn::launch_prefill_tc(p, ws, s);
         const cudaError_t ef = cudaFreeAsync(ws, s);
         if (e != cudaSuccess) return cuda_status(e, "gdn_prefill (tcgen05) launch");
-        return cuda_status(ef, "gdn_prefill (tcgen05) workspace release");
+        if (ef != cudaSuccess) return cuda_status(ef, "gdn_prefill (tcgen05) workspace release");
+        return gate_output(p, s);
     }
     const bool chunked_ok = gdn::prefill_chunked_supported(p);
     if (method == GDN_PREFILL_CHUNKED && !chunked_ok)
         return fail(GDN_ERR_UNSUPPORTED, "the chunked tensor-core prefill is not available here");
-    if (method == GDN_PREFILL_RECURRENT || (method == GDN_PREFILL_AUTO && !chunked_ok))
-        return cuda_status(gdn::launch_prefill_recurrent(p, s), "gdn_prefill (recurrent) launch");
-    return cuda_status(gdn::launch_prefill_chunked(p, s), "gdn_prefill (chunked) launch");
+    const bool recurrent = method == GDN_PREFILL_RECURRENT || (method == GDN_PREFILL_AUTO && !chunked_ok);
+    cudaError_t e = recurrent ? gdn::launch_prefill_recurrent(p, s) : gdn::launch_prefill_chunked(p, s);
+    if (e != cudaSuccess) return cuda_status(e, recurrent ? "gdn_prefill (recurrent) launch" : "gdn_prefill (chunked) launch");
+    return gate_output(p, s);
 }
 
 int gdn_prefill_ex(const void *q, const void *k, const void *v, const float *state,
@@ -255,6 +276,25 @@ int gdn_prefill_flags(const void *q, const void *k, const void *v, const float *
     return prefill_impl(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs, total_tokens,
                         num_qk_heads, num_v_heads, head_size, scale, gate_dtype, param_dtype, output,
                         new_state, method, nullptr, 0, stream, flags);
+}
+
+int gdn_prefill_gated(const void *q, const void *k, const void *v, const float *state,
+                      const void *A_log, const void *a, const void *dt_bias, const void *b,
+                      const int32_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
+                      int num_qk_heads, int num_v_heads, int head_size, float scale,
+                      int gate_dtype, int param_dtype, void *output, float *new_state,
+                      const void *out_gate, const void *norm_weight, int norm_weight_dtype, float eps,
+                      int method, int flags, void *stream) {
+    g_last_error[0] = '\0';
+    if (!out_gate || !norm_weight) return fail(GDN_ERR_INVALID_ARGUMENT, "null gate or norm weight");
+    if (!aligned16(out_gate)) return fail(GDN_ERR_INVALID_ARGUMENT, "gate must be 16-byte aligned");
+    if (norm_weight_dtype != GDN_DTYPE_F32 && norm_weight_dtype != GDN_DTYPE_BF16)
+        return fail(GDN_ERR_INVALID_ARGUMENT, "unknown norm_weight_dtype %d", norm_weight_dtype);
+    if (!(eps >= 0.0f)) return fail(GDN_ERR_INVALID_ARGUMENT, "eps must be >= 0");
+    return prefill_impl(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs, total_tokens,
+                        num_qk_heads, num_v_heads, head_size, scale, gate_dtype, param_dtype, output,
+                        new_state, method, nullptr, 0, stream, flags, out_gate, norm_weight, norm_weight_dtype,
+                        eps);
 }
 
 int gdn_prefill_ws(const void *q, const void *k, const void *v, const float *state,

@@ -44,6 +44,38 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     return *reinterpret_cast<uint32_t *>(&h);
 }
 
+// Gated RMSNorm of one 128-element bf16 vector held by an aligned group of 16 lanes,
+// 8 elements (one 16-byte word) each: o / sqrt(mean(o^2) + eps) * w * silu(z), fp32,
+// rounded to bf16.  ow / zw are this lane's words of o and z, wv its 8 weights.  Every
+// lane of the warp must call it (full-warp shuffles).
+__device__ __forceinline__ uint4 gated_rmsnorm16(uint4 ov, uint4 zv, const float (&wv)[8], float eps) {
+    const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w}, zw[4] = {zv.x, zv.y, zv.z, zv.w};
+    float x[8], g[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        x[2 * e] = bf16_lo(ow[e]); x[2 * e + 1] = bf16_hi(ow[e]);
+        g[2 * e] = bf16_lo(zw[e]); g[2 * e + 1] = bf16_hi(zw[e]);
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss = fmaf(x[e], x[e], ss);
+#pragma unroll
+    for (int m = 1; m < 16; m <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+    const float inv = 1.0f / sqrtf(ss * (1.0f / 128.0f) + eps);
+    uint32_t r[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        float y[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int i = 2 * e + u;
+            y[u] = x[i] * inv * wv[i] * (g[i] / (1.0f + expf(-g[i])));
+        }
+        r[e] = pack_bf16x2(y[0], y[1]);
+    }
+    return make_uint4(r[0], r[1], r[2], r[3]);
+}
+
 // Streaming (evict-first) 128-bit global accesses for data touched once.
 __device__ __forceinline__ float4 ld_stream(const float4 *p) { return __ldcs(p); }
 __device__ __forceinline__ void st_stream(float4 *p, float4 v) { __stcs(p, v); }

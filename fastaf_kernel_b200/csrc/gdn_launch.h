@@ -32,6 +32,12 @@ struct PrefillArgs {
     int gate_dtype, param_dtype;
     void *out;                   // bf16 [T, Hv, D]
     float *new_state;            // fp32 [N, Hv, D, D]
+    // Optional gated RMSNorm of the output (gate == nullptr: none): bf16 [T, Hv, D] gate,
+    // [D] weight (dtype code), eps; applied by a pass after the prefill kernels.
+    const void *out_gate = nullptr;
+    const void *norm_w = nullptr;
+    int norm_w_dtype = 0;
+    float norm_eps = 0.0f;
 };
 
 // Set the message gdn_last_error() returns on this thread.

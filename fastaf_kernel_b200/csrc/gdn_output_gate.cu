@@ -6,7 +6,8 @@
 //
 // per 128-element head vector, in fp32 from the bf16 o and z, rounded to bf16.  It
 // reads and writes the output once (in place); 16 lanes own one vector, 8 elements
-// (one 16-byte load) each, and reduce the sum of squares with a 16-lane butterfly.
+// (one 16-byte load) each, and reduce the sum of squares with a 16-lane butterfly
+// (gated_rmsnorm16, which the tcgen05 prefill's fused output store shares).
 #include "gdn_common.cuh"
 #include "gdn_launch.h"
 
@@ -23,33 +24,11 @@ output_gate_kernel(__nv_bfloat16 *__restrict__ o, const __nv_bfloat16 *__restric
     const int64_t base = (live ? vec : 0) * kHeadDim + l16 * 8;
     const uint4 ov = *reinterpret_cast<const uint4 *>(o + base);
     const uint4 zv = __ldg(reinterpret_cast<const uint4 *>(z + base));
-    const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w}, zw[4] = {zv.x, zv.y, zv.z, zv.w};
-    float x[8], g[8];
+    float wv[8];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-        x[2 * e] = bf16_lo(ow[e]); x[2 * e + 1] = bf16_hi(ow[e]);
-        g[2 * e] = bf16_lo(zw[e]); g[2 * e + 1] = bf16_hi(zw[e]);
-    }
-    float ss = 0.0f;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) ss = fmaf(x[e], x[e], ss);
-#pragma unroll
-    for (int m = 1; m < 16; m <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
-    const float inv = 1.0f / sqrtf(ss * (1.0f / kHeadDim) + eps);
-    uint32_t r[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-        float y[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const int i = 2 * e + u;
-            const float wi = load_scalar(w, l16 * 8 + i, w_dtype);
-            const float silu = g[i] / (1.0f + expf(-g[i]));
-            y[u] = x[i] * inv * wi * silu;
-        }
-        r[e] = pack_bf16x2(y[0], y[1]);
-    }
-    if (live) *reinterpret_cast<uint4 *>(o + base) = make_uint4(r[0], r[1], r[2], r[3]);
+    for (int i = 0; i < 8; ++i) wv[i] = load_scalar(w, l16 * 8 + i, w_dtype);
+    const uint4 y = gated_rmsnorm16(ov, zv, wv, eps);
+    if (live) *reinterpret_cast<uint4 *>(o + base) = y;
 }
 
 cudaError_t launch_output_gate(void *o, const void *z, const void *w, int w_dtype, int64_t vectors, float eps,

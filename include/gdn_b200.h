@@ -167,6 +167,17 @@ GDN_API int gdn_prefill_noalloc(const void *q, const void *k, const void *v, con
 GDN_API int gdn_output_gate(void *output, const void *gate, const void *weight, int weight_dtype,
                     int64_t num_vectors, int head_size, float eps, void *stream);
 
+/* gdn_prefill_flags followed by gdn_output_gate on the output, in one call (gate:
+ * bf16 [T, Hv, D], 16-byte aligned; norm_weight [D] in norm_weight_dtype).
+ * Bit-identical to the two calls.  No counterpart in the reference. */
+GDN_API int gdn_prefill_gated(const void *q, const void *k, const void *v, const float *state,
+                      const void *A_log, const void *a, const void *dt_bias, const void *b,
+                      const int32_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
+                      int num_qk_heads, int num_v_heads, int head_size, float scale,
+                      int gate_dtype, int param_dtype, void *output, float *new_state,
+                      const void *out_gate, const void *norm_weight, int norm_weight_dtype, float eps,
+                      int method, int flags, void *stream);
+
 /* The prefill kernel (GDN_PREFILL_*) a call with `method` runs for `total_tokens` packed
  * tokens on the current device: AUTO resolves to TCGEN05, CHUNKED or RECURRENT; other
  * values are returned unchanged.  No counterpart in the reference. */

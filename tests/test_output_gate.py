@@ -53,6 +53,21 @@ def test_prefill_with_output_gate(method):
     _assert_close(o_gated, _reference(o_plain, z, w, 1e-5))
 
 
+def test_gated_prefill_is_bit_identical_to_two_calls():
+    """kernel(..., output_gate=) (gdn_prefill_gated) equals prefill, then output_gate."""
+    x = W.prefill_inputs([700, 129, 64, 1], seed=73, Hq=4, Hv=8, device=DEV)
+    T = x["q"].shape[0]
+    g = torch.Generator(device=DEV).manual_seed(8)
+    z = torch.randn((T, 8, 128), generator=g, device=DEV).to(torch.bfloat16)
+    w = torch.rand(128, generator=g, device=DEV) + 0.5
+    args = (x["q"], x["k"], x["v"], x["state"], x["A_log"], x["a"], x["dt_bias"], x["b"], x["cu_seqlens"], x["scale"])
+    o_fused, _ = fk.kernel(*args, method="tcgen05", output_gate=z, norm_weight=w)
+    o_plain, _ = fk.kernel(*args, method="tcgen05")
+    fk.output_gate(o_plain, z, w)
+    fk.device_status()
+    assert torch.equal(o_fused, o_plain)
+
+
 def test_decode_with_output_gate():
     d = W.decode_inputs(16, seed=72, Hq=4, Hv=8, device=DEV)
     g = torch.Generator(device=DEV).manual_seed(7)
