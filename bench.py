@@ -211,7 +211,7 @@ def main():
     # ---------------- prefill: inputs resident in HBM ----------------
     x = W.prefill_long(seed=3 + rank, device=dev)
     T = N_SEQS * SEQ_LEN
-    kernel_name = fk.prefill_method(T, args.method)
+    kernel_name = fk.prefill_method(T, args.method, N_SEQS)
     # the tcgen05 path is two launches per step (chunk prep, then the chains)
     launches_per_step = 2 if kernel_name == "tcgen05" else 1
     out = torch.empty((T, 32, 128), dtype=torch.bfloat16, device=dev)

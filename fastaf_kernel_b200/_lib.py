@@ -77,7 +77,7 @@ def load() -> ctypes.CDLL:
         lib.gdn_prefill_ws.restype = i32
         lib.gdn_prefill_noalloc.argtypes = prefill_args + [vp]
         lib.gdn_prefill_noalloc.restype = i32
-        lib.gdn_prefill_resolve.argtypes = [i64, i32]
+        lib.gdn_prefill_resolve.argtypes = [i64, i64, i32]
         lib.gdn_prefill_resolve.restype = i32
         lib.gdn_prefill_workspace_size.argtypes = [i64, i64, i32]
         lib.gdn_prefill_workspace_size.restype = ctypes.c_size_t

@@ -41,12 +41,13 @@ _METHODS = {"auto": _lib.GDN_PREFILL_AUTO, "chunked": _lib.GDN_PREFILL_CHUNKED,
             "recurrent": _lib.GDN_PREFILL_RECURRENT, "tcgen05": _lib.GDN_PREFILL_TCGEN05}
 
 
-def prefill_method(total_tokens: int, method: str = "auto") -> str:
+def prefill_method(total_tokens: int, method: str = "auto", num_seqs: int = 1) -> str:
     """Name of the prefill kernel a call with ``method`` runs for ``total_tokens``
-    packed tokens on the current CUDA device (the C library's own choice)."""
+    packed tokens in ``num_seqs`` sequences on the current CUDA device (the C
+    library's own choice)."""
     if method not in _METHODS:
         raise ValueError(f"method must be one of {sorted(_METHODS)}")
-    code = _lib.load().gdn_prefill_resolve(int(total_tokens), _METHODS[method])
+    code = _lib.load().gdn_prefill_resolve(int(total_tokens), int(num_seqs), _METHODS[method])
     return {v: k for k, v in _METHODS.items()}[code]
 
 

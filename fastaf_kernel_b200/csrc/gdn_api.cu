@@ -21,6 +21,7 @@ thread_local char g_last_error[512] = "";
 // on B200 (256 tokens 43 vs 51 us, 1024 tokens 56 vs 84 us at Hq 16 / Hv 32); below it
 // the extra prep launch does not pay off (64-128 tokens: 42 vs 32 us).
 constexpr int64_t kAutoTcMinTokens = 256;
+constexpr int64_t kAutoRecurrentMaxTokens = 32;
 
 int fail(int code, const char *fmt, ...) {
     va_list ap;
@@ -221,10 +222,8 @@ static int prefill_impl(const void *q, const void *k, const void *v, const float
         if (rc2 != GDN_OK) return rc2;
         return cuda_status(ef, "gdn_prefill (qk l2norm) scratch release");
     }
-    // auto: the tcgen05 pipeline from kAutoTcMinTokens tokens; below that its extra prep
-    // launch does not pay off and the single-launch mma.sync kernel is faster.
-    if (method == GDN_PREFILL_AUTO && gdn_prefill_resolve(total_tokens, method) == GDN_PREFILL_TCGEN05)
-        method = GDN_PREFILL_TCGEN05;
+    // auto: gdn_prefill_resolve's choice
+    if (method == GDN_PREFILL_AUTO) method = gdn_prefill_resolve(total_tokens, num_seqs, method);
     if (method == GDN_PREFILL_TCGEN05) {
         if (!gdn::prefill_tc_supported(p))
             return fail(GDN_ERR_UNSUPPORTED,
@@ -325,10 +324,16 @@ int gdn_output_gate(void *output, const void *gate, const void *weight, int weig
                        "gdn_output_gate launch");
 }
 
-int gdn_prefill_resolve(int64_t total_tokens, int method) {
+int gdn_prefill_resolve(int64_t total_tokens, int64_t num_seqs, int method) {
     gdn::PrefillArgs p{};
     p.total_tokens = total_tokens;
+    p.num_seqs = num_seqs;
     if (method == GDN_PREFILL_AUTO) {
+        // Tiny batches and batches of very short sequences: the token-serial fp32 kernel
+        // costs the same or less there (T <= 32: equal; 64 sequences of 1 token: 101 vs
+        // 210 us) and follows the reference's fp32 recurrence exactly, also on inputs
+        // with unnormalised keys that amplify the state.
+        if (total_tokens <= kAutoRecurrentMaxTokens || total_tokens < 4 * num_seqs) return GDN_PREFILL_RECURRENT;
         if (total_tokens >= kAutoTcMinTokens && gdn::prefill_tc_supported(p)) return GDN_PREFILL_TCGEN05;
         return gdn::prefill_chunked_supported(p) ? GDN_PREFILL_CHUNKED : GDN_PREFILL_RECURRENT;
     }

@@ -47,7 +47,7 @@ extern "C" {
 #define GDN_FLAG_QK_L2NORM 1   /* L2-normalise every q and k head vector first (see below) */
 
 /* Prefill kernel choice for gdn_prefill_ex(). */
-#define GDN_PREFILL_AUTO 0      /* TCGEN05 from 256 packed tokens, else CHUNKED, else RECURRENT */
+#define GDN_PREFILL_AUTO 0      /* see gdn_prefill_resolve() */
 #define GDN_PREFILL_CHUNKED 1   /* chunked (C=64) WY/UT kernel on the tensor cores (mma.sync) */
 #define GDN_PREFILL_RECURRENT 2 /* token-serial CUDA-core kernel */
 #define GDN_PREFILL_TCGEN05 3   /* chunked (C=64) kernel on tcgen05 + TMEM + TMA; T >= 64 */
@@ -179,9 +179,11 @@ GDN_API int gdn_prefill_gated(const void *q, const void *k, const void *v, const
                       int method, int flags, void *stream);
 
 /* The prefill kernel (GDN_PREFILL_*) a call with `method` runs for `total_tokens` packed
- * tokens on the current device: AUTO resolves to TCGEN05, CHUNKED or RECURRENT; other
- * values are returned unchanged.  No counterpart in the reference. */
-GDN_API int gdn_prefill_resolve(int64_t total_tokens, int method);
+ * tokens in `num_seqs` sequences on the current device: AUTO resolves to RECURRENT for
+ * at most 32 tokens or fewer than 4 tokens per sequence, else to TCGEN05 from 256
+ * tokens, else CHUNKED; other values are returned unchanged.  No counterpart in the
+ * reference. */
+GDN_API int gdn_prefill_resolve(int64_t total_tokens, int64_t num_seqs, int method);
 
 /* Workspace bytes gdn_prefill_ws needs for GDN_PREFILL_TCGEN05:
  * (ceil(total_tokens / 64) + num_seqs) * num_v_heads * 41984.  No counterpart in the reference. */

@@ -181,12 +181,25 @@ def test_prefill_output_destination_passing():
 
 
 def test_auto_method_resolution():
-    """auto runs the tcgen05 pipeline from 256 packed tokens, the mma.sync kernel below."""
+    """auto: the tcgen05 pipeline from 256 packed tokens, the mma.sync kernel below, the
+    token-serial kernel for at most 32 tokens or under 4 tokens per sequence."""
     assert fk.prefill_method(256) == "tcgen05"
-    assert fk.prefill_method(131072) == "tcgen05"
+    assert fk.prefill_method(131072, num_seqs=16) == "tcgen05"
     assert fk.prefill_method(255) == "chunked"
-    assert fk.prefill_method(1) == "chunked"
+    assert fk.prefill_method(33) == "chunked"
+    assert fk.prefill_method(32) == "recurrent"
+    assert fk.prefill_method(1) == "recurrent"
+    assert fk.prefill_method(300, num_seqs=100) == "recurrent"
     assert fk.prefill_method(5000, "recurrent") == "recurrent"
+
+
+def test_prefill_reference_test_fixture_auto():
+    """The reference test's fixture (T = 17, unnormalised keys) through auto, which
+    picks the token-serial fp32 kernel for it."""
+    name = "prefill_qk4_v8_t17"
+    g = fixtures.load(name)
+    o, s = _prefill(fixtures.make_inputs(name), "auto")
+    assert _golden_state(g, s) <= 1e-3
 
 
 def test_prefill_caller_workspace():
