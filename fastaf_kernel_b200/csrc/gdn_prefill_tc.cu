@@ -31,7 +31,8 @@
 //               in TMEM, then the previous chunk's output rows from O^T in TMEM
 //   warps 5-12  state path, two halves of four warps: S -> hi/lo split and decay, the
 //               innovation split
-// The fp32 state lives in TMEM columns [0,128) for the whole sequence.
+// The fp32 state lives in TMEM columns [0,128) for the whole sequence.  The barrier
+// protocol is modelled on the CPU under random schedules (tests/test_tc_chain_protocol.py).
 //
 // Every wait is bounded (about 2 s).  A wait that gives up records its site in
 // g_tc_error and raises a shared abort flag; every role then stops at its next wait,

@@ -1,0 +1,460 @@
+"""CPU model of the mbarrier protocol of the tcgen05 chain kernel
+(fastaf_kernel_b200/csrc/gdn_prefill_tc.cu), run under random schedules.
+
+The kernel hands every chunk between five roles -- the MMA-issuing thread, the copy
+thread, four prep warps and eight state warps -- through mbarriers only (no block-wide
+barrier in the chunk loop).  The model runs each warp as a coroutine that follows the
+kernel's waits, reads, writes and arrives in the kernel's order; MMA batches and
+copies are asynchronous events.  The tensor pipe is in order (tcgen05.mma and
+tcgen05.commit issued by one thread complete in issue order, a commit arriving once
+every earlier MMA is done); copies land in any order and complete their barrier's
+transaction count.
+
+Each schedule checks:
+  * no deadlock: every role finishes and every asynchronous operation completes;
+  * every parity wait on the k-th completion of a barrier is evaluated while the
+    barrier has completed k or k + 1 phases (k - 1 would pass early on the previous
+    phase of the same parity; k + 2 would have lapped it);
+  * every read sees the chunk and stage of the data it expects (buffers carry tags);
+  * no warp writes a buffer, and no copy is issued into one, while an asynchronous
+    operation that reads or writes it is in flight; no MMA batch is issued on an
+    operand whose copy is still in flight.
+Buffers: shared-memory stages (K, Q, V, P, gates) x 2, the T' and T'' tiles, -W hi/lo
+and (Gamma Q)^T (per TMEM lane quadrant of the warp that writes them); TMEM S (per
+state half and quadrant), the [128, 256) hi/lo/delta region in 16-column blocks,
+W^T, [U | X] and O^T (per quadrant).
+
+Two protocol variants are modelled: ``serial`` (the S update, the S split and the
+delta batch each wait for all of the previous step) and ``pipelined`` (the S update
+is issued as two 64-column halves with a commit after the first, the state halves
+split S as soon as their half is final, and the delta batch goes out in two halves of
+the contraction, each behind its half of the split).  The kernel's barrier counts are
+read from the source and compared with the model's.  Planted protocol mistakes (a
+missing condition or wait) must be caught.
+"""
+import os
+import random
+import re
+
+import pytest
+
+KERNEL = os.path.join(os.path.dirname(__file__), "..", "fastaf_kernel_b200", "csrc", "gdn_prefill_tc.cu")
+
+
+class ProtocolError(AssertionError):
+    pass
+
+
+class Bar:
+    """mbarrier: `count` arrivals plus a transaction byte count per phase."""
+
+    def __init__(self, name, count):
+        self.name, self.count = name, count
+        self.pending, self.tx, self.done = count, 0, 0
+
+    def _complete(self):
+        if self.pending == 0 and self.tx == 0:
+            self.done += 1
+            self.pending = self.count
+
+    def arrive(self, tx=0):
+        self.tx += tx
+        self.pending -= 1
+        self._complete()
+
+    def complete_tx(self, n):
+        self.tx -= n
+        self._complete()
+
+    def test(self, k, where):
+        """Hardware parity test for the k-th completion (0-based), with the invariant."""
+        p = self.done
+        if p < k or p > k + 1:
+            raise ProtocolError(f"{where}: wait for completion {k} of {self.name} evaluated after {p}")
+        return (p & 1) != (k & 1)
+
+
+class Sim:
+    def __init__(self, nch, variant, plant=None):
+        self.nch, self.variant, self.plant = nch, variant, plant
+        self.tags = {}
+        self.copy_w = {}      # part -> in-flight copies writing it
+        self.mma_r = {}       # part -> in-flight MMA batches reading it
+        self.mma_w = {}       # part -> in-flight MMA batches writing it
+        self.pipe = []        # in-order tensor pipe: ("mma", reads, writes) / ("commit", bar)
+        self.copies = []      # in-flight copies: (part, tag, bar)
+        counts = dict(tma0=1, tma1=1, wdone=1, udone=1, d=1, s=1, qs=4, w=4, ds=8, tw=1, tu=1,
+                      free0=1, free1=1, oread=4)
+        if variant == "pipelined":
+            counts.update(sa=1, ss0=4, ss1=4)
+        else:
+            counts.update(ss=8)
+        self.counts = counts
+        self.b = {k: Bar(k, v) for k, v in counts.items()}
+
+    # ---------------------------------------------------------------- data
+    @staticmethod
+    def _inc(d, p):
+        d[p] = d.get(p, 0) + 1
+
+    @staticmethod
+    def _dec(d, p):
+        d[p] -= 1
+
+    def read(self, part, tag, who):
+        if self.copy_w.get(part) or self.mma_w.get(part):
+            raise ProtocolError(f"{who} reads {part} while an async write of it is in flight")
+        if self.tags.get(part) != tag:
+            raise ProtocolError(f"{who} reads {part}: holds {self.tags.get(part)}, expected {tag}")
+
+    def write(self, part, tag, who):
+        if self.copy_w.get(part) or self.mma_w.get(part) or self.mma_r.get(part):
+            raise ProtocolError(f"{who} writes {part} while an async access of it is in flight")
+        self.tags[part] = tag
+
+    def mma(self, reads, writes, who):
+        """reads: {part: tag}; writes: {part: (expected previous tag or None, new tag)}."""
+        for p in list(reads) + list(writes):
+            if self.copy_w.get(p):
+                raise ProtocolError(f"{who} issued while the copy of {p} is in flight")
+        for p in reads:
+            self._inc(self.mma_r, p)
+        for p in writes:
+            self._inc(self.mma_w, p)
+        self.pipe.append(("mma", reads, writes, who))
+
+    def commit(self, bar):
+        self.pipe.append(("commit", self.b[bar]))
+
+    def copy(self, parts, tag, bar, who):
+        b = self.b[bar]
+        b.arrive(tx=len(parts))
+        for p in parts:
+            if self.copy_w.get(p) or self.mma_r.get(p) or self.mma_w.get(p):
+                raise ProtocolError(f"{who}: copy into {p} while an async access of it is in flight")
+            self._inc(self.copy_w, p)
+            self.copies.append((p, tag, b))
+
+    def retire_pipe(self):
+        e = self.pipe.pop(0)
+        if e[0] == "commit":
+            e[1].arrive()
+            return
+        _, reads, writes, who = e
+        for p, t in reads.items():
+            if self.tags.get(p) != t:
+                raise ProtocolError(f"{who} executes on {p} = {self.tags.get(p)}, expected {t}")
+        for p, (prev, t) in writes.items():
+            if prev is not None and self.tags.get(p) != prev:
+                raise ProtocolError(f"{who} accumulates into {p} = {self.tags.get(p)}, expected {prev}")
+        for p in reads:
+            self._dec(self.mma_r, p)
+        for p, (_, t) in writes.items():
+            self._dec(self.mma_w, p)
+            self.tags[p] = t
+
+    def retire_copy(self, i):
+        p, tag, b = self.copies.pop(i)
+        self._dec(self.copy_w, p)
+        self.tags[p] = tag
+        b.complete_tx(1)
+
+
+Q4 = range(4)
+
+
+def _stage(st):
+    return [(x, st) for x in ("K", "Q", "V", "P", "G")]
+
+
+def _r(blocks, tag):
+    return {("R", bl, q): tag for bl in blocks for q in Q4}
+
+
+# ------------------------------------------------------------------ MMA batches
+def mma6w(sim, c):   # W^T = K^T T''^T
+    st = c & 1
+    sim.mma({("K", st): c, ("T2",): c}, {("W", q): (None, c) for q in Q4}, f"W^T({c})")
+    sim.commit("wdone")
+
+
+def mma6u(sim, c):   # [U | X] = V^T [T'_hi | T'_lo]^T
+    st = c & 1
+    sim.mma({("V", st): c, ("T1",): c}, {("UX", q): (None, ("u", c)) for q in Q4}, f"U({c})")
+    sim.commit("udone")
+
+
+def _delta_b_operands(c):
+    return {**{("WH", q): c for q in Q4}, **{("WL", q): c for q in Q4}, **{("QS", q): c for q in Q4}}
+
+
+def mma8(sim, c):    # [U | X | O] += S_hi [-W_hi | -W_lo | Gamma Q]^T; U += S_lo (-W_hi)^T
+    reads = {**_r(range(8), ("Ssplit", c)), **_delta_b_operands(c)}
+    writes = {**{("UX", q): (("u", c), ("delta", c)) for q in Q4},
+              **{("O", q): (("zero", c), ("qs", c)) for q in Q4}}
+    sim.mma(reads, writes, f"delta({c})")
+    sim.commit("d")
+
+
+def mma8a(sim, c):   # first half of the contraction (state columns 0..63)
+    reads = {**_r(range(4), ("Ssplit", c)), **_delta_b_operands(c)}
+    writes = {**{("UX", q): (("u", c), ("delta_a", c)) for q in Q4},
+              **{("O", q): (("zero", c), ("qs_a", c)) for q in Q4}}
+    sim.mma(reads, writes, f"delta_a({c})")
+
+
+def mma8b(sim, c):   # second half (state columns 64..127)
+    reads = {**_r(range(4, 8), ("Ssplit", c)), **_delta_b_operands(c)}
+    writes = {**{("UX", q): (("delta_a", c), ("delta", c)) for q in Q4},
+              **{("O", q): (("qs_a", c), ("qs", c)) for q in Q4}}
+    sim.mma(reads, writes, f"delta_b({c})")
+    sim.commit("d")
+
+
+def mma10(sim, c):   # S += delta'^T K, O^T += delta^T P^T
+    st = c & 1
+    reads = {**_r(range(6), ("dsplit", c)), ("K", st): c, ("P", st): c}
+    writes = {**{("S", hs, q): (("Sdec", c), ("S", c + 1)) for hs in (0, 1) for q in Q4},
+              **{("O", q): (("qs", c), ("out", c)) for q in Q4}}
+    sim.mma(reads, writes, f"S update({c})")
+    sim.commit("s")
+    sim.commit(f"free{st}")
+
+
+def mma10p(sim, c):  # pipelined: state columns 0..63 and O^T, commit; columns 64..127, commit
+    st = c & 1
+    reads = {**_r((0, 1, 4, 5, 6, 7), ("dsplit", c)), ("K", st): c, ("P", st): c}
+    writes = {**{("S", 0, q): (("Sdec", c), ("S", c + 1)) for q in Q4},
+              **{("O", q): (("qs", c), ("out", c)) for q in Q4}}
+    sim.mma(reads, writes, f"S update a({c})")
+    sim.commit("sa")
+    reads = {**_r((4, 5, 6, 7), ("dsplit", c)), ("K", st): c}
+    writes = {("S", 1, q): (("Sdec", c), ("S", c + 1)) for q in Q4}
+    sim.mma(reads, writes, f"S update b({c})")
+    sim.commit("s")
+    sim.commit(f"free{st}")
+
+
+# ------------------------------------------------------------------ roles
+def issuer(sim):
+    b, nch, plant = sim.b, sim.nch, sim.plant
+    n6w = n6u = n8 = n10 = n8a = 0
+    pipelined = sim.variant == "pipelined"
+    while n10 < nch:
+        progress = False
+        if n10 < n8 and b["ds"].test(n10, "issue S update"):
+            (mma10p if pipelined else mma10)(sim, n10)
+            n10 += 1
+            progress = True
+        if pipelined:
+            if (n8a == n8 and n8a < n6u and b["ss0"].test(n8a, "issue delta a")
+                    and b["w"].test(n8a, "issue delta a") and b["qs"].test(n8a, "issue delta a")
+                    and (n8a == 0 or plant == "no_oread" or b["oread"].test(n8a - 1, "issue delta a"))):
+                mma8a(sim, n8a)
+                n8a += 1
+                progress = True
+            if n8 < n8a and b["ss1"].test(n8, "issue delta b"):
+                mma8b(sim, n8)
+                n8 += 1
+                progress = True
+        elif (n8 < n6u and b["ss"].test(n8, "issue delta") and b["w"].test(n8, "issue delta")
+              and b["qs"].test(n8, "issue delta")
+              and (n8 == 0 or plant == "no_oread" or b["oread"].test(n8 - 1, "issue delta"))):
+            mma8(sim, n8)
+            n8 += 1
+            progress = True
+        if (n6w < nch and (n6w <= n8 or plant == "w_early") and b["tw"].test(n6w, "issue W")
+                and b[f"tma{n6w & 1}"].test(n6w >> 1, "issue W")):
+            mma6w(sim, n6w)
+            n6w += 1
+            progress = True
+        if n6u < n6w and (n6u <= n10 or plant == "u_early") and b["tu"].test(n6u, "issue U"):
+            mma6u(sim, n6u)
+            n6u += 1
+            progress = True
+        sim.progress = progress
+        yield "spin"
+    for bar, n in (("wdone", n6w), ("udone", n6u), ("d", n8), ("s", n10)):
+        if n:
+            yield ("wait", bar, n - 1)
+    for c in range(max(0, n10 - 2), n10):
+        yield ("wait", f"free{c & 1}", c >> 1)
+
+
+def copier(sim):
+    for c in range(sim.nch):
+        st = c & 1
+        if c >= 1:
+            yield ("wait", "wdone", c - 1)
+        sim.copy([("T2",)], c, "tw", f"copy T''({c})")
+        if c >= 2 and sim.plant != "no_free_wait":
+            yield ("wait", f"free{st}", (c - 2) >> 1)
+        sim.copy(_stage(st), c, f"tma{st}", f"copy stage({c})")
+        if c >= 1:
+            yield ("wait", "udone", c - 1)
+        sim.copy([("T1",)], c, "tu", f"copy T'({c})")
+        yield None
+
+
+def prep(sim, q):
+    who = f"prep{q}"
+    out_bar = "sa" if sim.variant == "pipelined" else "s"
+
+    def write_out(c):
+        sim.read(("O", q), ("out", c), who)
+        yield None
+        sim.write(("O", q), ("zero", c + 1), who)
+        sim.b["oread"].arrive()
+        yield None
+
+    for c in range(sim.nch):
+        st = c & 1
+        yield ("wait", f"tma{st}", c >> 1)
+        if c > 0:
+            yield ("wait", "d", c - 1)
+        sim.read(("G", st), c, who)
+        sim.read(("Q", st), c, who)
+        yield None
+        sim.write(("QS", q), c, who)
+        if c == 0:
+            sim.write(("O", q), ("zero", 0), who)
+        yield None
+        sim.b["qs"].arrive()
+        yield ("wait", "wdone", c)
+        sim.read(("W", q), c, who)
+        yield None
+        sim.write(("WH", q), c, who)
+        sim.write(("WL", q), c, who)
+        yield None
+        sim.b["w"].arrive()
+        if c > 0:
+            yield ("wait", out_bar, c - 1)
+            yield from write_out(c - 1)
+    if sim.nch:
+        yield ("wait", out_bar, sim.nch - 1)
+        yield from write_out(sim.nch - 1)
+
+
+def state(sim, hs, q):
+    who = f"state{hs}.{q}"
+    pipelined = sim.variant == "pipelined"
+    if pipelined:
+        split_blocks = (0, 1, 2, 3) if hs == 0 else (4, 5, 6, 7)
+        delta_blocks = (hs, 4 + hs, 6 + hs)
+        s_bar = "sa" if hs == 0 or sim.plant == "half1_on_sa" else "s"
+        ss_bar = f"ss{hs}"
+    else:
+        split_blocks = (2 * hs, 2 * hs + 1, 4 + 2 * hs, 5 + 2 * hs)
+        delta_blocks = (hs, 2 + hs, 4 + hs)
+        s_bar, ss_bar = "s", "ss"
+    sim.write(("S", hs, q), ("S", 0), who)
+    yield None
+    for c in range(sim.nch):
+        st = c & 1
+        if c > 0:
+            yield ("wait", s_bar, c - 1)
+        yield ("wait", f"tma{st}", c >> 1)
+        sim.read(("G", st), c, who)
+        sim.read(("S", hs, q), ("S", c), who)
+        yield None
+        for bl in split_blocks:
+            sim.write(("R", bl, q), ("Ssplit", c), who)
+        sim.write(("S", hs, q), ("Sdec", c), who)
+        yield None
+        sim.b[ss_bar].arrive()
+        yield ("wait", "d", c)
+        sim.read(("UX", q), ("delta", c), who)
+        sim.read(("G", st), c, who)
+        yield None
+        for bl in delta_blocks:
+            sim.write(("R", bl, q), ("dsplit", c), who)
+        yield None
+        sim.b["ds"].arrive()
+    if sim.nch:
+        yield ("wait", "s", sim.nch - 1)
+        sim.read(("S", hs, q), ("S", sim.nch), who)
+
+
+def run(nch, seed, variant, plant=None, max_steps=400000):
+    sim = Sim(nch, variant, plant)
+    rng = random.Random(seed)
+    roles = {"issuer": issuer(sim), "copier": copier(sim)}
+    roles.update({f"prep{q}": prep(sim, q) for q in Q4})
+    roles.update({f"state{hs}.{q}": state(sim, hs, q) for hs in (0, 1) for q in Q4})
+    waiting = {}    # role -> (bar, k)
+    done = set()
+
+    def step(name):
+        try:
+            r = next(roles[name])
+        except StopIteration:
+            done.add(name)
+            return
+        if isinstance(r, tuple) and r[0] == "wait":
+            waiting[name] = (r[1], r[2])
+
+    for _ in range(max_steps):
+        live = [n for n in roles if n not in done]
+        if not live and not sim.pipe and not sim.copies:
+            return sim
+        ready = []
+        for n in live:
+            if n == "issuer" and n not in waiting:
+                continue
+            if n in waiting:
+                bar, k = waiting[n]
+                if not sim.b[bar].test(k, n):
+                    continue
+            ready.append(("role", n))
+        if sim.pipe:
+            ready.append(("pipe", None))
+        ready += [("copy", i) for i in range(len(sim.copies))]
+        spinning = "issuer" in live and "issuer" not in waiting
+        if not ready and not spinning:
+            raise ProtocolError(f"deadlock: waiting {waiting}")
+        if spinning and (not ready or rng.random() < 0.3):
+            step("issuer")
+            if not ready and not sim.progress and "issuer" not in done and "issuer" not in waiting:
+                raise ProtocolError(f"deadlock (issuer idle): waiting {waiting}")
+            continue
+        kind, x = ready[rng.randrange(len(ready))]
+        if kind == "pipe":
+            sim.retire_pipe()
+        elif kind == "copy":
+            sim.retire_copy(x)
+        else:
+            waiting.pop(x, None)
+            step(x)
+    raise ProtocolError("schedule did not finish")
+
+
+CHUNKS = [1, 2, 3, 4, 5, 8, 17]
+
+
+@pytest.mark.parametrize("variant", ["serial", "pipelined"])
+@pytest.mark.parametrize("nch", CHUNKS)
+def test_protocol_random_schedules(variant, nch):
+    for seed in range(40):
+        sim = run(nch, 1000 * nch + seed, variant)
+        for hs in (0, 1):
+            for q in Q4:
+                assert sim.tags[("S", hs, q)] == ("S", nch)
+
+
+@pytest.mark.parametrize("variant,plant", [
+    ("serial", "w_early"), ("serial", "u_early"), ("serial", "no_free_wait"), ("serial", "no_oread"),
+    ("pipelined", "w_early"), ("pipelined", "u_early"), ("pipelined", "no_free_wait"),
+    ("pipelined", "no_oread"), ("pipelined", "half1_on_sa"),
+])
+def test_planted_protocol_mistakes_are_caught(variant, plant):
+    with pytest.raises(ProtocolError):
+        for seed in range(200):
+            run(5, seed, variant, plant)
+
+
+def test_barrier_counts_match_the_kernel():
+    """The kernel's mbar_init counts equal the model's (the variant the source uses)."""
+    src = open(KERNEL).read()
+    inits = {name[2:]: int(n) for name, n in re.findall(r"mbar_init\((b_\w+), (\d+)\)", src)}
+    variant = "pipelined" if "sa" in inits else "serial"
+    assert inits == Sim(1, variant).counts
