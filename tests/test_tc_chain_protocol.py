@@ -24,13 +24,8 @@ and (Gamma Q)^T (per TMEM lane quadrant of the warp that writes them); TMEM S (p
 state half and quadrant), the [128, 256) hi/lo/delta region in 16-column blocks,
 W^T, [U | X] and O^T (per quadrant).
 
-Two protocol variants are modelled: ``serial`` (the S update, the S split and the
-delta batch each wait for all of the previous step) and ``pipelined`` (the S update
-is issued as two 64-column halves with a commit after the first, the state halves
-split S as soon as their half is final, and the delta batch goes out in two halves of
-the contraction, each behind its half of the split).  The kernel's barrier counts are
-read from the source and compared with the model's.  Planted protocol mistakes (a
-missing condition or wait) must be caught.
+The kernel's barrier counts are read from the source and compared with the model's.
+Planted protocol mistakes (a missing condition or wait) must be caught.
 """
 import os
 import random
@@ -75,20 +70,16 @@ class Bar:
 
 
 class Sim:
-    def __init__(self, nch, variant, plant=None):
-        self.nch, self.variant, self.plant = nch, variant, plant
+    def __init__(self, nch, plant=None):
+        self.nch, self.plant = nch, plant
         self.tags = {}
         self.copy_w = {}      # part -> in-flight copies writing it
         self.mma_r = {}       # part -> in-flight MMA batches reading it
         self.mma_w = {}       # part -> in-flight MMA batches writing it
         self.pipe = []        # in-order tensor pipe: ("mma", reads, writes) / ("commit", bar)
         self.copies = []      # in-flight copies: (part, tag, bar)
-        counts = dict(tma0=1, tma1=1, wdone=1, udone=1, d=1, s=1, qs=4, w=4, ds=8, tw=1, tu=1,
+        counts = dict(tma0=1, tma1=1, wdone=1, udone=1, d=1, s=1, qs=4, w=4, ss=8, ds=8, tw=1, tu=1,
                       free0=1, free1=1, oread=4)
-        if variant == "pipelined":
-            counts.update(sa=1, ss0=4, ss1=4)
-        else:
-            counts.update(ss=8)
         self.counts = counts
         self.b = {k: Bar(k, v) for k, v in counts.items()}
 
@@ -196,21 +187,6 @@ def mma8(sim, c):    # [U | X | O] += S_hi [-W_hi | -W_lo | Gamma Q]^T; U += S_l
     sim.commit("d")
 
 
-def mma8a(sim, c):   # first half of the contraction (state columns 0..63)
-    reads = {**_r(range(4), ("Ssplit", c)), **_delta_b_operands(c)}
-    writes = {**{("UX", q): (("u", c), ("delta_a", c)) for q in Q4},
-              **{("O", q): (("zero", c), ("qs_a", c)) for q in Q4}}
-    sim.mma(reads, writes, f"delta_a({c})")
-
-
-def mma8b(sim, c):   # second half (state columns 64..127)
-    reads = {**_r(range(4, 8), ("Ssplit", c)), **_delta_b_operands(c)}
-    writes = {**{("UX", q): (("delta_a", c), ("delta", c)) for q in Q4},
-              **{("O", q): (("qs_a", c), ("qs", c)) for q in Q4}}
-    sim.mma(reads, writes, f"delta_b({c})")
-    sim.commit("d")
-
-
 def mma10(sim, c):   # S += delta'^T K, O^T += delta^T P^T
     st = c & 1
     reads = {**_r(range(6), ("dsplit", c)), ("K", st): c, ("P", st): c}
@@ -221,43 +197,17 @@ def mma10(sim, c):   # S += delta'^T K, O^T += delta^T P^T
     sim.commit(f"free{st}")
 
 
-def mma10p(sim, c):  # pipelined: state columns 0..63 and O^T, commit; columns 64..127, commit
-    st = c & 1
-    reads = {**_r((0, 1, 4, 5, 6, 7), ("dsplit", c)), ("K", st): c, ("P", st): c}
-    writes = {**{("S", 0, q): (("Sdec", c), ("S", c + 1)) for q in Q4},
-              **{("O", q): (("qs", c), ("out", c)) for q in Q4}}
-    sim.mma(reads, writes, f"S update a({c})")
-    sim.commit("sa")
-    reads = {**_r((4, 5, 6, 7), ("dsplit", c)), ("K", st): c}
-    writes = {("S", 1, q): (("Sdec", c), ("S", c + 1)) for q in Q4}
-    sim.mma(reads, writes, f"S update b({c})")
-    sim.commit("s")
-    sim.commit(f"free{st}")
-
-
 # ------------------------------------------------------------------ roles
 def issuer(sim):
     b, nch, plant = sim.b, sim.nch, sim.plant
-    n6w = n6u = n8 = n10 = n8a = 0
-    pipelined = sim.variant == "pipelined"
+    n6w = n6u = n8 = n10 = 0
     while n10 < nch:
         progress = False
         if n10 < n8 and b["ds"].test(n10, "issue S update"):
-            (mma10p if pipelined else mma10)(sim, n10)
+            mma10(sim, n10)
             n10 += 1
             progress = True
-        if pipelined:
-            if (n8a == n8 and n8a < n6u and b["ss0"].test(n8a, "issue delta a")
-                    and b["w"].test(n8a, "issue delta a") and b["qs"].test(n8a, "issue delta a")
-                    and (n8a == 0 or plant == "no_oread" or b["oread"].test(n8a - 1, "issue delta a"))):
-                mma8a(sim, n8a)
-                n8a += 1
-                progress = True
-            if n8 < n8a and b["ss1"].test(n8, "issue delta b"):
-                mma8b(sim, n8)
-                n8 += 1
-                progress = True
-        elif (n8 < n6u and b["ss"].test(n8, "issue delta") and b["w"].test(n8, "issue delta")
+        if (n8 < n6u and b["ss"].test(n8, "issue delta") and b["w"].test(n8, "issue delta")
               and b["qs"].test(n8, "issue delta")
               and (n8 == 0 or plant == "no_oread" or b["oread"].test(n8 - 1, "issue delta"))):
             mma8(sim, n8)
@@ -298,7 +248,7 @@ def copier(sim):
 
 def prep(sim, q):
     who = f"prep{q}"
-    out_bar = "sa" if sim.variant == "pipelined" else "s"
+    out_bar = "s"
 
     def write_out(c):
         sim.read(("O", q), ("out", c), who)
@@ -337,16 +287,9 @@ def prep(sim, q):
 
 def state(sim, hs, q):
     who = f"state{hs}.{q}"
-    pipelined = sim.variant == "pipelined"
-    if pipelined:
-        split_blocks = (0, 1, 2, 3) if hs == 0 else (4, 5, 6, 7)
-        delta_blocks = (hs, 4 + hs, 6 + hs)
-        s_bar = "sa" if hs == 0 or sim.plant == "half1_on_sa" else "s"
-        ss_bar = f"ss{hs}"
-    else:
-        split_blocks = (2 * hs, 2 * hs + 1, 4 + 2 * hs, 5 + 2 * hs)
-        delta_blocks = (hs, 2 + hs, 4 + hs)
-        s_bar, ss_bar = "s", "ss"
+    split_blocks = (2 * hs, 2 * hs + 1, 4 + 2 * hs, 5 + 2 * hs)
+    delta_blocks = (hs, 2 + hs, 4 + hs)
+    s_bar, ss_bar = "s", "ss"
     sim.write(("S", hs, q), ("S", 0), who)
     yield None
     for c in range(sim.nch):
@@ -375,8 +318,8 @@ def state(sim, hs, q):
         sim.read(("S", hs, q), ("S", sim.nch), who)
 
 
-def run(nch, seed, variant, plant=None, max_steps=400000):
-    sim = Sim(nch, variant, plant)
+def run(nch, seed, plant=None, max_steps=400000):
+    sim = Sim(nch, plant)
     rng = random.Random(seed)
     roles = {"issuer": issuer(sim), "copier": copier(sim)}
     roles.update({f"prep{q}": prep(sim, q) for q in Q4})
@@ -431,30 +374,24 @@ def run(nch, seed, variant, plant=None, max_steps=400000):
 CHUNKS = [1, 2, 3, 4, 5, 8, 17]
 
 
-@pytest.mark.parametrize("variant", ["serial", "pipelined"])
 @pytest.mark.parametrize("nch", CHUNKS)
-def test_protocol_random_schedules(variant, nch):
-    for seed in range(40):
-        sim = run(nch, 1000 * nch + seed, variant)
+def test_protocol_random_schedules(nch):
+    for seed in range(60):
+        sim = run(nch, 1000 * nch + seed)
         for hs in (0, 1):
             for q in Q4:
                 assert sim.tags[("S", hs, q)] == ("S", nch)
 
 
-@pytest.mark.parametrize("variant,plant", [
-    ("serial", "w_early"), ("serial", "u_early"), ("serial", "no_free_wait"), ("serial", "no_oread"),
-    ("pipelined", "w_early"), ("pipelined", "u_early"), ("pipelined", "no_free_wait"),
-    ("pipelined", "no_oread"), ("pipelined", "half1_on_sa"),
-])
-def test_planted_protocol_mistakes_are_caught(variant, plant):
+@pytest.mark.parametrize("plant", ["w_early", "u_early", "no_free_wait", "no_oread"])
+def test_planted_protocol_mistakes_are_caught(plant):
     with pytest.raises(ProtocolError):
         for seed in range(200):
-            run(5, seed, variant, plant)
+            run(5, seed, plant)
 
 
 def test_barrier_counts_match_the_kernel():
-    """The kernel's mbar_init counts equal the model's (the variant the source uses)."""
+    """The kernel's mbar_init counts equal the model's."""
     src = open(KERNEL).read()
     inits = {name[2:]: int(n) for name, n in re.findall(r"mbar_init\((b_\w+), (\d+)\)", src)}
-    variant = "pipelined" if "sa" in inits else "serial"
-    assert inits == Sim(1, variant).counts
+    assert inits == Sim(1).counts
