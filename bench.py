@@ -212,8 +212,15 @@ def main():
     x = W.prefill_long(seed=3 + rank, device=dev)
     T = N_SEQS * SEQ_LEN
     kernel_name = fk.prefill_method(T, args.method, N_SEQS)
-    # the tcgen05 path is two launches per step (chunk prep, then the chains)
-    launches_per_step = 2 if kernel_name == "tcgen05" else 1
+    # the tcgen05 path is two launches per step (chunk prep, then the chains), four when
+    # the library splits off the last partial wave of chains onto its second stream (the
+    # rule of launch_prefill_tc: more chains than SMs, chains mod SMs > 0 and a multiple
+    # of the v-heads one prep CTA serves)
+    launches_per_step = 1
+    if kernel_name == "tcgen05":
+        chains, sms = N_SEQS * 32, torch.cuda.get_device_properties(dev).multi_processor_count
+        tail = chains % sms
+        launches_per_step = 4 if chains > sms and tail > 0 and tail % 2 == 0 else 2
     out = torch.empty((T, 32, 128), dtype=torch.bfloat16, device=dev)
     ns = torch.empty((N_SEQS, 32, 128, 128), dtype=torch.float32, device=dev)
 

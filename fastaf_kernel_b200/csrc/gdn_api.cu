@@ -240,7 +240,7 @@ static int prefill_impl(const void *q, const void *k, const void *v, const float
         void *ws = nullptr;
         cudaError_t e = pool_alloc(&ws, need, s);
         if (e != cudaSuccess) return cuda_status(e, "gdn_prefill (tcgen05) workspace");
-        e = gdn::launch_prefill_tc(p, ws, s);
+        e = gdn::launch_prefill_tc(p, ws, s, /*overlap=*/true);
         const cudaError_t ef = cudaFreeAsync(ws, s);
         if (e != cudaSuccess) return cuda_status(e, "gdn_prefill (tcgen05) launch");
         if (ef != cudaSuccess) return cuda_status(ef, "gdn_prefill (tcgen05) workspace release");

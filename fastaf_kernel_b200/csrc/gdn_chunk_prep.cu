@@ -68,6 +68,7 @@ struct PrepParams {
     uint8_t *ws_T;
     float *ws_g;
     __nv_bfloat16 *ws_P;
+    int64_t group0;   // (sequence, v-head group) index of blockIdx.x = 0
 };
 
 // [64][128] bf16 rows t0.. of head hh into 256-byte swizzled rows; rows past T read
@@ -148,7 +149,7 @@ __global__ void __launch_bounds__(kThreads, 4) chunk_prep_kernel(const PrepParam
     extern __shared__ __align__(1024) uint8_t sm[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t4 = lane & 3;
-    const int64_t chain = blockIdx.x;                  // (sequence, group of NH v-heads)
+    const int64_t chain = blockIdx.x + p.group0;       // (sequence, group of NH v-heads)
     const int hgroups = p.Hv / NH;
     const int64_t n = chain / hgroups;
     const int h0 = static_cast<int>(chain % hgroups) * NH;
@@ -426,11 +427,18 @@ int prep_groups(int64_t chains) {
     return static_cast<int>(gsz < 1 ? 1 : (gsz > 64 ? 64 : gsz));
 }
 
-cudaError_t launch_chunk_prep(const PrefillArgs &p, uint8_t *ws_T, __nv_bfloat16 *ws_P, float *ws_g,
-                              cudaStream_t stream) {
+int prep_heads_per_cta(const PrefillArgs &p) {
     // Two v-heads per CTA when the v-heads of every q/k head pair up.
-    const int nh = ((p.Hv / p.Hq) % 2 == 0) ? 2 : 1;
-    const int64_t chains = p.num_seqs * (p.Hv / nh);
+    return ((p.Hv / p.Hq) % 2 == 0) ? 2 : 1;
+}
+
+cudaError_t launch_chunk_prep(const PrefillArgs &p, uint8_t *ws_T, __nv_bfloat16 *ws_P, float *ws_g,
+                              cudaStream_t stream, int64_t chain_begin, int64_t chain_end) {
+    const int nh = prep_heads_per_cta(p);
+    if (chain_end < 0) chain_end = p.num_seqs * p.Hv;
+    if (chain_begin % nh != 0 || chain_end % nh != 0 || chain_begin > chain_end)
+        return cudaErrorInvalidValue;
+    const int64_t chains = (chain_end - chain_begin) / nh;
     if (chains == 0) return cudaSuccess;
     if (chains > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
     const int groups = prep_groups(chains);
@@ -440,7 +448,7 @@ cudaError_t launch_chunk_prep(const PrefillArgs &p, uint8_t *ws_T, __nv_bfloat16
     if (e != cudaSuccess) return e;
     PrepParams pp{static_cast<const __nv_bfloat16 *>(p.q), static_cast<const __nv_bfloat16 *>(p.k), p.A_log,
                   p.a, p.dt_bias, p.b, p.cu_seqlens, p.total_tokens, p.Hq, p.Hv, groups, p.gate_dtype,
-                  p.param_dtype, ws_T, ws_g, ws_P};
+                  p.param_dtype, ws_T, ws_g, ws_P, chain_begin / nh};
     kernel<<<dim3(static_cast<unsigned>(chains), groups), kThreads, smem, stream>>>(pp);
     return cudaGetLastError();
 }

@@ -56,11 +56,19 @@ cudaError_t launch_prefill_chunked(const PrefillArgs &p, cudaStream_t stream);
 bool prefill_chunked_supported(const PrefillArgs &p);
 // tcgen05 prefill: per-chunk prep (gdn_chunk_prep.cu) into `workspace` of
 // prefill_tc_workspace_bytes() bytes (256-byte aligned), then the chain kernel.
-cudaError_t launch_prefill_tc(const PrefillArgs &p, void *workspace, cudaStream_t stream);
+// With `overlap`, a call of more chains than the device has SMs whose last partial wave
+// would leave SMs idle is split in two: the last (chains mod SMs) chains -- prep and
+// chain kernels -- on a library-owned high-priority stream, the rest on `stream`, so the
+// short group's chains run while the rest is being prepped (fork and join through
+// events; same kernels, same results).
+cudaError_t launch_prefill_tc(const PrefillArgs &p, void *workspace, cudaStream_t stream, bool overlap = false);
 bool prefill_tc_supported(const PrefillArgs &p);
 size_t prefill_tc_workspace_bytes(const PrefillArgs &p);
+// Prep of the chains (sequence-major (sequence, v-head) indices) [chain_begin, chain_end)
+// (chain_end < 0: to the last chain); both multiples of prep_heads_per_cta(p).
 cudaError_t launch_chunk_prep(const PrefillArgs &p, uint8_t *ws_T, __nv_bfloat16 *ws_P, float *ws_g,
-                              cudaStream_t stream);
+                              cudaStream_t stream, int64_t chain_begin = 0, int64_t chain_end = -1);
+int prep_heads_per_cta(const PrefillArgs &p);
 // Site of the first bounded device wait of the tcgen05 prefill that gave up (0 = none).
 cudaError_t read_tc_device_error(cudaStream_t stream, int *code, bool clear);
 

@@ -40,6 +40,7 @@
 // the CTA frees TMEM and exits.
 #include <cuda_bf16.h>
 #include <cstring>
+#include <mutex>
 
 #include "gdn_chunk_common.cuh"
 #include "gdn_common.cuh"
@@ -109,6 +110,7 @@ struct TcParams {
     const uint8_t *ws_T;
     const float *ws_g;
     const __nv_bfloat16 *ws_P;
+    int64_t chain0;   // (sequence, v-head) chain of blockIdx.x = 0
 };
 
 struct Bars {
@@ -176,7 +178,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t lane_base = static_cast<uint32_t>(warp & 3) * 32;
     const int row = static_cast<int>(lane_base) + lane;    // this thread's TMEM lane (warps 1-8)
-    const int64_t chain = blockIdx.x;
+    const int64_t chain = blockIdx.x + p.chain0;
     const int64_t n = chain / p.Hv;
     const int h = static_cast<int>(chain % p.Hv);
     const int hq = h / (p.Hv / p.Hq);
@@ -610,8 +612,54 @@ size_t prefill_tc_workspace_bytes(const PrefillArgs &p) {
     return static_cast<size_t>(tc_workspace_bytes(p.total_tokens, p.num_seqs, p.Hv));
 }
 
-// Two launches on `stream`: the per-chunk prep of every chunk, then the chains.
-cudaError_t launch_prefill_tc(const PrefillArgs &p, void *workspace, cudaStream_t stream) {
+namespace {
+
+// The library's second stream of a device (highest priority) and its fork / join events,
+// created on first use and kept until exit; `mu` serialises the fork-join enqueue.
+struct OverlapStream {
+    cudaStream_t aux = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+    int sms = 0;
+    bool tried = false;
+};
+constexpr int kMaxDevices = 64;
+OverlapStream g_overlap[kMaxDevices];
+std::mutex g_overlap_mu;
+
+// (with g_overlap_mu held) the device's overlap stream, or nullptr when it cannot be had.
+OverlapStream *overlap_stream(cudaStream_t stream) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    OverlapStream &o = g_overlap[dev];
+    if (!o.tried) {
+        // Not created inside a stream capture (creation is then left to a later call).
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return nullptr;
+        o.tried = true;
+        int lo = 0, hi = 0;
+        if (cudaDeviceGetStreamPriorityRange(&lo, &hi) != cudaSuccess ||
+            cudaDeviceGetAttribute(&o.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+            cudaStreamCreateWithPriority(&o.aux, cudaStreamNonBlocking, hi) != cudaSuccess ||
+            cudaEventCreateWithFlags(&o.fork, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&o.join, cudaEventDisableTiming) != cudaSuccess) {
+            cudaGetLastError();
+            o.aux = nullptr;
+            return nullptr;
+        }
+    }
+    return o.aux ? &o : nullptr;
+}
+
+}  // namespace
+
+// The prep and chain kernels of every chain on `stream`, or -- with `overlap`, more
+// chains than SMs and a partial last wave -- the last (chains mod SMs) chains on the
+// high-priority overlap stream and the rest on `stream`: the block scheduler then runs
+// the short group's chains on part of the GPU while the other group is being prepped,
+// and the long group's chains fill whole waves.  The chain kernel takes one SM per chain
+// (all 512 TMEM columns), so without the split the last wave of a batch of equal-length
+// chains leaves (SMs - chains mod SMs) SMs idle for a whole chain length.
+cudaError_t launch_prefill_tc(const PrefillArgs &p, void *workspace, cudaStream_t stream, bool overlap) {
     const int64_t ctas = p.num_seqs * p.Hv;
     if (ctas == 0) return cudaSuccess;
     if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
@@ -628,14 +676,33 @@ cudaError_t launch_prefill_tc(const PrefillArgs &p, void *workspace, cudaStream_
         !make_tmap_thd_bf16(&km, p.k, p.total_tokens, p.Hq) ||
         !make_tmap_thd_bf16(&vm, p.v, p.total_tokens, p.Hv))
         return cudaErrorInvalidValue;
-    cudaError_t e = launch_chunk_prep(p, ws_T, ws_P, ws_g, stream);
+    cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    TcParams tp{p.state, p.cu_seqlens, p.total_tokens, p.Hq, p.Hv, p.scale,
-                static_cast<__nv_bfloat16 *>(p.out), p.new_state, ws_T, ws_g, ws_P};
-    prefill_tc_kernel<<<static_cast<unsigned>(ctas), kThreads, SMEM_BYTES, stream>>>(qm, km, vm, tp);
-    return cudaGetLastError();
+    // prep + chains of [c0, c1) on stream st
+    auto launch_range = [&](int64_t c0, int64_t c1, cudaStream_t st) -> cudaError_t {
+        cudaError_t er = launch_chunk_prep(p, ws_T, ws_P, ws_g, st, c0, c1);
+        if (er != cudaSuccess) return er;
+        TcParams tp{p.state, p.cu_seqlens, p.total_tokens, p.Hq, p.Hv, p.scale,
+                    static_cast<__nv_bfloat16 *>(p.out), p.new_state, ws_T, ws_g, ws_P, c0};
+        prefill_tc_kernel<<<static_cast<unsigned>(c1 - c0), kThreads, SMEM_BYTES, st>>>(qm, km, vm, tp);
+        return cudaGetLastError();
+    };
+    if (overlap) {
+        std::lock_guard<std::mutex> lock(g_overlap_mu);
+        OverlapStream *o = overlap_stream(stream);
+        if (o && ctas > o->sms) {
+            const int64_t tail = ctas % o->sms;
+            if (tail > 0 && tail % prep_heads_per_cta(p) == 0) {
+                if ((e = cudaEventRecord(o->fork, stream)) != cudaSuccess) return e;
+                if ((e = cudaStreamWaitEvent(o->aux, o->fork, 0)) != cudaSuccess) return e;
+                if ((e = launch_range(ctas - tail, ctas, o->aux)) != cudaSuccess) return e;
+                if ((e = cudaEventRecord(o->join, o->aux)) != cudaSuccess) return e;
+                if ((e = launch_range(0, ctas - tail, stream)) != cudaSuccess) return e;
+                return cudaStreamWaitEvent(stream, o->join, 0);
+            }
+        }
+    }
+    return launch_range(0, ctas, stream);
 }
 
 cudaError_t read_tc_device_error(cudaStream_t stream, int *code, bool clear) {

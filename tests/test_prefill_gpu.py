@@ -233,3 +233,67 @@ def test_prefill_caller_workspace():
     assert small == _lib.GDN_ERR_INVALID_ARGUMENT
     fk.device_status()
     assert torch.equal(out, o_ref) and torch.equal(ns, s_ref)
+
+
+def _ws_call(g, N, Hq, Hv):
+    """The tcgen05 prefill through gdn_prefill_ws (caller workspace: one stream, no split)."""
+    from fastaf_kernel_b200 import _lib
+    lib = _lib.load()
+    T = g["q"].shape[0]
+    nbytes = lib.gdn_prefill_workspace_size(N, T, Hv)
+    ws = torch.empty((nbytes,), dtype=torch.uint8, device=DEV)
+    out = torch.empty((T, Hv, 128), dtype=torch.bfloat16, device=DEV)
+    ns = torch.empty((N, Hv, 128, 128), dtype=torch.float32, device=DEV)
+    st = g["state"]
+    rc = lib.gdn_prefill_ws(g["q"].data_ptr(), g["k"].data_ptr(), g["v"].data_ptr(),
+                            None if st is None else st.data_ptr(), g["A_log"].data_ptr(), g["a"].data_ptr(),
+                            g["dt_bias"].data_ptr(), g["b"].data_ptr(), g["cu_seqlens"].data_ptr(), N, T, Hq, Hv,
+                            128, float(g["scale"]), _lib.GDN_DTYPE_BF16, _lib.GDN_DTYPE_F32, out.data_ptr(),
+                            ns.data_ptr(), _lib.GDN_PREFILL_TCGEN05, ws.data_ptr(), nbytes,
+                            torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, lib.gdn_last_error()
+    return out, ns
+
+
+@pytest.mark.parametrize("lengths,Hq,Hv", [
+    ([300, 128, 257, 64, 200], 16, 32),                       # 160 chains: two v-heads per prep CTA
+    ([90, 64, 130, 70, 65, 200, 64, 100, 64, 77, 64, 150, 64], 4, 12),   # 156 chains: one per prep CTA
+    ([256, 0, 191, 64, 300], 16, 32),                         # an empty sequence among them
+])
+def test_prefill_tc_wave_split_matches_single_stream(lengths, Hq, Hv):
+    """A batch of more chains than SMs with a partial last wave: the pooled call splits the
+    last (chains mod SMs) chains onto the library's second stream; the result is bit-for-bit
+    that of the one-stream launch (caller workspace) and within tolerance of the oracle."""
+    sms = torch.cuda.get_device_properties(DEV).multi_processor_count
+    chains = len(lengths) * Hv
+    assert chains > sms and chains % sms > 0, "the case must exercise the split"
+    x = W.prefill_inputs(lengths, seed=33, Hq=Hq, Hv=Hv)
+    g = _gpu(x)
+    o, s = fk.kernel(g["q"], g["k"], g["v"], g["state"], g["A_log"], g["a"], g["dt_bias"], g["b"],
+                     g["cu_seqlens"], g["scale"], method="tcgen05")
+    o1, s1 = _ws_call(g, len(lengths), Hq, Hv)
+    fk.device_status()
+    assert torch.equal(o, o1) and torch.equal(s, s1)
+    ro, rs = _oracle(x)
+    assert_parity(o.cpu(), ro, s.cpu(), rs)
+
+
+def test_prefill_tc_wave_split_under_graph_capture():
+    """The split launch (fork onto the library's second stream, join back) records into a
+    CUDA graph, and replaying it reproduces the eager result."""
+    x = W.prefill_inputs([300, 128, 257, 64, 200], seed=34)
+    g = _gpu(x)
+    run = lambda: fk.kernel(g["q"], g["k"], g["v"], g["state"], g["A_log"], g["a"], g["dt_bias"], g["b"],
+                            g["cu_seqlens"], g["scale"], method="tcgen05", validate=False)
+    o, s = run()
+    torch.cuda.synchronize()
+    cs = torch.cuda.Stream()
+    cs.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=cs):
+        og, sg = run()
+    graph.replay()
+    torch.cuda.synchronize()
+    fk.device_status()
+    assert torch.equal(og, o) and torch.equal(sg, s)
+    del graph
