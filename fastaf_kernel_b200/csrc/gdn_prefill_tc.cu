@@ -408,9 +408,15 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             const int nt = static_cast<int>(s1 - t0 < kC ? s1 - t0 : kC);
             __nv_bfloat16 *so = reinterpret_cast<__nv_bfloat16 *>(sm + OFF_O);
             named_sync(2, 128);   // the previous chunk's rows have left the staging tile
+            // two tokens per packed conversion (the single-value one runs at a quarter of the
+            // rate and these warps share their SMSPs with the state split)
+            uint16_t *so16 = reinterpret_cast<uint16_t *>(so);
 #pragma unroll
-            for (int ii = 0; ii < 64; ++ii)
-                so[ii * kHeadDim + row] = __float2bfloat16_rn(p.scale * __uint_as_float(o[ii]));
+            for (int ii = 0; ii < 64; ii += 2) {
+                const uint32_t pk = pack_bf16x2(p.scale * __uint_as_float(o[ii]), p.scale * __uint_as_float(o[ii + 1]));
+                so16[ii * kHeadDim + row] = static_cast<uint16_t>(pk);
+                so16[(ii + 1) * kHeadDim + row] = static_cast<uint16_t>(pk >> 16);
+            }
             named_sync(2, 128);
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
