@@ -640,7 +640,11 @@ OverlapStream *overlap_stream(cudaStream_t stream) {
     if (!o.tried) {
         // Not created inside a stream capture (creation is then left to a later call).
         cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-        if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return nullptr;
+        if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess) {
+            cudaGetLastError();   // (not left pending for the launch's own error check)
+            return nullptr;
+        }
+        if (cs != cudaStreamCaptureStatusNone) return nullptr;
         o.tried = true;
         int lo = 0, hi = 0;
         if (cudaDeviceGetStreamPriorityRange(&lo, &hi) != cudaSuccess ||
