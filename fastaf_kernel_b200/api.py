@@ -26,6 +26,7 @@ unchanged:
 
 from __future__ import annotations
 
+import contextlib
 import math
 from typing import Optional, Tuple
 
@@ -56,12 +57,21 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
 
 
 def _require_cuda(name: str, t: torch.Tensor, device: torch.device) -> None:
+    # (integer device indices: cheaper than building torch.device objects on every call)
     if not isinstance(t, torch.Tensor):
         raise TypeError(f"{name} must be a torch.Tensor")
-    if t.device.type != "cuda":
+    if not t.is_cuda:
         raise ValueError(f"{name} must be a CUDA tensor (there is no CPU path), got {t.device}")
-    if t.device != device:
+    if t.get_device() != device.index:
         raise ValueError(f"{name} is on {t.device}, expected {device}")
+
+
+def _on_device(device: torch.device):
+    """(context making ``device`` current, its current stream's raw handle); the context
+    is a no-op when ``device`` is already current (the common case: no device switch)."""
+    if device.index == torch.cuda.current_device():
+        return contextlib.nullcontext(), torch.cuda.current_stream().cuda_stream
+    return torch.cuda.device(device), torch.cuda.current_stream(device).cuda_stream
 
 
 def _bf16(name: str, t: torch.Tensor) -> torch.Tensor:
@@ -164,8 +174,8 @@ def kernel(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: Optional[to
         raise ValueError(f"method must be one of {sorted(_METHODS)}")
 
     lib = _lib.load()
-    with torch.cuda.device(device):
-        stream = torch.cuda.current_stream(device).cuda_stream
+    ctx, stream = _on_device(device)
+    with ctx:
         flags = _lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm else 0
         if output_gate is None and norm_weight is None:
             _lib.check(lib.gdn_prefill_flags(
@@ -242,8 +252,8 @@ def kernel_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         raise ValueError("new_state must be a contiguous fp32 [B, Hv, D, D] tensor on q's device")
 
     lib = _lib.load()
-    with torch.cuda.device(device):
-        stream = torch.cuda.current_stream(device).cuda_stream
+    ctx, stream = _on_device(device)
+    with ctx:
         _lib.check(lib.gdn_decode_flags(
             _ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias),
             _ptr(b), B, Hq, Hv, D, scale, _GATE_DTYPES[a.dtype], _GATE_DTYPES[A_log.dtype],
@@ -288,8 +298,8 @@ def _gated_rmsnorm(output, gate, weight, eps):
     device = output.device
     D = output.shape[-1]
     lib = _lib.load()
-    with torch.cuda.device(device):
-        stream = torch.cuda.current_stream(device).cuda_stream
+    ctx, stream = _on_device(device)
+    with ctx:
         _lib.check(lib.gdn_output_gate(_ptr(output), _ptr(gate), _ptr(weight), _GATE_DTYPES[weight.dtype],
                                        output.numel() // D, D, float(eps), stream))
     return output
