@@ -5,7 +5,7 @@ Drop-in for the reference's ``kernel`` / ``kernel_decode`` entry points
 ``libgdn_b200.so`` (C ABI: include/gdn_b200.h).
 """
 
-from .api import (device_status, kernel, kernel_decode, kernel_dps, kernel_decode_dps,  # noqa: F401
-                  output_gate, prefill_method)
+from .api import (decode_step, device_status, kernel, kernel_decode, kernel_dps,  # noqa: F401
+                  kernel_decode_dps, output_gate, prefill_method)
 
 __version__ = "0.1.0"

@@ -129,3 +129,43 @@ def test_decode_steps_equal_prefill():
     torch.cuda.synchronize()
     assert_parity(torch.cat(outs).cpu(), po.cpu(), st.cpu(), ps.cpu(), state_tol=1e-5,
                   atol=1e-2, rtol=1e-2)
+
+
+def test_decode_step_matches_kernel_decode():
+    """A prepared decode step over fixed buffers (refilled in place every token, state
+    updated in place) gives bit for bit what kernel_decode gives, and creating it launches
+    nothing."""
+    B, Hq, Hv = 8, 16, 32
+    x = W.decode_inputs(B, seed=71, Hq=Hq, Hv=Hv, device=DEV)
+    bufs = {k2: x[k2].clone() for k2 in ("q", "k", "v", "a", "b")}
+    state = x["state"].clone()
+    ref_state = x["state"].clone()
+    out = torch.empty((B, 1, Hv, 128), dtype=torch.bfloat16, device=DEV)
+    step = fk.decode_step(bufs["q"], bufs["k"], bufs["v"], state, x["A_log"], bufs["a"], x["dt_bias"],
+                          bufs["b"], x["scale"], out, state)
+    torch.cuda.synchronize()
+    assert torch.equal(state, x["state"]), "creating the step must not run it"
+    for s in range(3):
+        d = W.decode_step_inputs(B, seed=100 + s, Hq=Hq, Hv=Hv, device=DEV)
+        for k2 in bufs:
+            bufs[k2].copy_(d[k2])
+        step()
+        ro, _ = fk.kernel_decode(d["q"], d["k"], d["v"], ref_state, x["A_log"], d["a"], x["dt_bias"], d["b"],
+                                 x["scale"], new_state=ref_state)
+        fk.device_status()
+        assert torch.equal(out, ro) and torch.equal(state, ref_state)
+
+
+def test_decode_step_needs_direct_buffers():
+    """Buffers that kernel_decode would copy (a strided q, a and b of different dtypes)
+    cannot back a prepared step."""
+    x = W.decode_inputs(2, seed=72, device=DEV)
+    out = torch.empty((2, 1, 32, 128), dtype=torch.bfloat16, device=DEV)
+    q_strided = torch.empty((2, 1, 16, 256), dtype=torch.bfloat16, device=DEV)[..., :128]
+    q_strided.copy_(x["q"])
+    with pytest.raises(ValueError, match="decode_step"):
+        fk.decode_step(q_strided, x["k"], x["v"], x["state"], x["A_log"], x["a"], x["dt_bias"], x["b"],
+                       x["scale"], out, x["state"])
+    with pytest.raises(ValueError, match="decode_step"):
+        fk.decode_step(x["q"], x["k"], x["v"], x["state"], x["A_log"], x["a"].float(), x["dt_bias"], x["b"],
+                       x["scale"], out, x["state"])

@@ -21,6 +21,14 @@ def test_no_cpu_path_decode():
                          x["dt_bias"], x["b"], x["scale"])
 
 
+def test_no_cpu_path_decode_step():
+    x = workloads.decode_inputs(2, seed=0, Hq=4, Hv=8)
+    out = torch.empty((2, 1, 8, 128), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        fk.decode_step(x["q"], x["k"], x["v"], x["state"], x["A_log"], x["a"], x["dt_bias"],
+                       x["b"], x["scale"], out, x["state"])
+
+
 def test_scale_default_matches_reference():
     # solution/triton/kernel.py:438-439
     assert kmod._scale(0.0, 128) == pytest.approx(128 ** -0.5)
