@@ -16,10 +16,45 @@ __device__ __forceinline__ void split_bf16(float x, float &hi, float &lo) {
 
 // The same split for two values at once, packed (a in bits 0-15): hi = bf16(a, b)
 // rounded to nearest even, lo = bf16 of the exact fp32 remainders.
+// Two fp32 lanes in one 64-bit register for sm_100's packed f32x2 arithmetic: one
+// instruction does two IEEE round-to-nearest operations, with the results of two scalar ones.
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void unf2(uint64_t v, float &lo, float &hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t add_f2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t sub_f2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t mul_f2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
 __device__ __forceinline__ void split2_bf16(float a, float b, uint32_t &hi, uint32_t &lo) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     hi = *reinterpret_cast<uint32_t *>(&h);
     __nv_bfloat162 l = __floats2bfloat162_rn(a - __uint_as_float(hi << 16), b - __uint_as_float(hi & 0xffff0000u));
+    lo = *reinterpret_cast<uint32_t *>(&l);
+}
+// The same split with the two remainders in one packed subtraction (identical results).
+__device__ __forceinline__ void split2_bf16_f2(float a, float b, uint32_t &hi, uint32_t &lo) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    hi = *reinterpret_cast<uint32_t *>(&h);
+    float la, lb;
+    unf2(sub_f2(f2(a, b), f2(__uint_as_float(hi << 16), __uint_as_float(hi & 0xffff0000u))), la, lb);
+    __nv_bfloat162 l = __floats2bfloat162_rn(la, lb);
     lo = *reinterpret_cast<uint32_t *>(&l);
 }
 

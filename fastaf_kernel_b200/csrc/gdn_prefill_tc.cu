@@ -413,7 +413,9 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             uint16_t *so16 = reinterpret_cast<uint16_t *>(so);
 #pragma unroll
             for (int ii = 0; ii < 64; ii += 2) {
-                const uint32_t pk = pack_bf16x2(p.scale * __uint_as_float(o[ii]), p.scale * __uint_as_float(o[ii + 1]));
+                float o0, o1;
+                unf2(mul_f2(f2(__uint_as_float(o[ii]), __uint_as_float(o[ii + 1])), f2(p.scale, p.scale)), o0, o1);
+                const uint32_t pk = pack_bf16x2(o0, o1);
                 so16[ii * kHeadDim + row] = static_cast<uint16_t>(pk);
                 so16[(ii + 1) * kHeadDim + row] = static_cast<uint16_t>(pk >> 16);
             }
@@ -475,7 +477,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                     uint32_t wh[4], wl[4];
 #pragma unroll
                     for (int e = 0; e < 4; ++e)
-                        split2_bf16(-__uint_as_float(r[cq * 8 + 2 * e]), -__uint_as_float(r[cq * 8 + 2 * e + 1]),
+                        split2_bf16_f2(-__uint_as_float(r[cq * 8 + 2 * e]), -__uint_as_float(r[cq * 8 + 2 * e + 1]),
                                     wh[e], wl[e]);
                     const uint32_t off = sw128(row, 4 * hf + cq);
                     *reinterpret_cast<uint4 *>(sm + OFF_WH + off) = make_uint4(wh[0], wh[1], wh[2], wh[3]);
@@ -533,11 +535,17 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                     tmem_wait_ld_dep(r);
 #pragma unroll
                     for (int j = 0; j < 16; ++j)
-                        split2_bf16(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]), hi[j], lo[j]);
+                        split2_bf16_f2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]), hi[j], lo[j]);
                     tmem_st16(tmem_addr(tm, lane_base, TM_SHI + 16 * q4), hi);
                     tmem_st16(tmem_addr(tm, lane_base, TM_SLO + 16 * q4), lo);
+                    const uint64_t g2 = f2(GamC, GamC);
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * GamC);
+                    for (int j = 0; j < 32; j += 2) {
+                        float s0, s1;
+                        unf2(mul_f2(f2(__uint_as_float(r[j]), __uint_as_float(r[j + 1])), g2), s0, s1);
+                        r[j] = __float_as_uint(s0);
+                        r[j + 1] = __float_as_uint(s1);
+                    }
                     tmem_st32(tmem_addr(tm, lane_base, TM_S + 32 * q4), r);
                     tmem_wait_st();
                 }
@@ -555,10 +563,13 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
                     const int i0 = hs * 32 + 2 * e, i1 = i0 + 1;
-                    const float d0 = __uint_as_float(r[2 * e]) + __uint_as_float(x[2 * e]);
-                    const float d1 = __uint_as_float(r[2 * e + 1]) + __uint_as_float(x[2 * e + 1]);
+                    const uint64_t d2 = add_f2(f2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1])),
+                                               f2(__uint_as_float(x[2 * e]), __uint_as_float(x[2 * e + 1])));
+                    float d0, d1, e0, e1;
+                    unf2(d2, d0, d1);
                     db[e] = pack_bf16x2(d0, d1);
-                    split2_bf16(d0 * g_dec[i0], d1 * g_dec[i1], dh[e], dl[e]);
+                    unf2(mul_f2(d2, f2(g_dec[i0], g_dec[i1])), e0, e1);
+                    split2_bf16_f2(e0, e1, dh[e], dl[e]);
                 }
                 tmem_st16(tmem_addr(tm, lane_base, TM_DBF + 16 * hs), db);
                 tmem_st16(tmem_addr(tm, lane_base, TM_DPH + 16 * hs), dh);
