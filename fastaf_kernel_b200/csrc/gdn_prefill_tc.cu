@@ -450,7 +450,9 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                         const float q0 = __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(src + sw128(i, kc)));
                         const float q1 =
                             __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(src + sw128(i + 1, kc)));
-                        w[e] = pack_bf16x2(q0 * g_Gam[i], q1 * g_Gam[i + 1]);
+                        float s0, s1;
+                        unf2(mul_f2(f2(q0, q1), f2(g_Gam[i], g_Gam[i + 1])), s0, s1);
+                        w[e] = pack_bf16x2(s0, s1);
                     }
                     *reinterpret_cast<uint4 *>(sm + OFF_QS + sw128(pt, ch)) = make_uint4(w[0], w[1], w[2], w[3]);
                 }
@@ -476,9 +478,14 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                 for (int cq = 0; cq < 4; ++cq) {
                     uint32_t wh[4], wl[4];
 #pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        split2_bf16_f2(-__uint_as_float(r[cq * 8 + 2 * e]), -__uint_as_float(r[cq * 8 + 2 * e + 1]),
-                                    wh[e], wl[e]);
+                    for (int e = 0; e < 4; ++e) {
+                        // hi/lo of -W = hi/lo of W with both packed signs flipped (the
+                        // rounding is symmetric)
+                        split2_bf16_f2(__uint_as_float(r[cq * 8 + 2 * e]), __uint_as_float(r[cq * 8 + 2 * e + 1]),
+                                       wh[e], wl[e]);
+                        wh[e] ^= 0x80008000u;
+                        wl[e] ^= 0x80008000u;
+                    }
                     const uint32_t off = sw128(row, 4 * hf + cq);
                     *reinterpret_cast<uint4 *>(sm + OFF_WH + off) = make_uint4(wh[0], wh[1], wh[2], wh[3]);
                     *reinterpret_cast<uint4 *>(sm + OFF_WL + off) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
