@@ -214,13 +214,12 @@ def main():
     kernel_name = fk.prefill_method(T, args.method, N_SEQS)
     # the tcgen05 path is two launches per step (chunk prep, then the chains), four when
     # the library splits off the last partial wave of chains onto its second stream (the
-    # rule of launch_prefill_tc: more chains than SMs, chains mod SMs > 0 and a multiple
-    # of the v-heads one prep CTA serves)
+    # library's own rule, gdn_prefill_tc_launches)
     launches_per_step = 1
     if kernel_name == "tcgen05":
-        chains, sms = N_SEQS * 32, torch.cuda.get_device_properties(dev).multi_processor_count
-        tail = chains % sms
-        launches_per_step = 4 if chains > sms and tail > 0 and tail % 2 == 0 else 2
+        from fastaf_kernel_b200 import _lib
+        launches_per_step = _lib.load().gdn_prefill_tc_launches(
+            N_SEQS, 16, 32, torch.cuda.get_device_properties(dev).multi_processor_count)
     out = torch.empty((T, 32, 128), dtype=torch.bfloat16, device=dev)
     ns = torch.empty((N_SEQS, 32, 128, 128), dtype=torch.float32, device=dev)
 

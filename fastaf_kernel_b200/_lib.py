@@ -31,7 +31,7 @@ GDN_FLAG_QK_L2NORM = 1
 
 # Every symbol include/gdn_b200.h declares.
 EXPORTED_SYMBOLS = ("gdn_prefill", "gdn_prefill_ex", "gdn_prefill_ws", "gdn_prefill_workspace_size",
-                    "gdn_prefill_resolve", "gdn_prefill_noalloc", "gdn_prefill_flags",
+                    "gdn_prefill_resolve", "gdn_prefill_tc_launches", "gdn_prefill_noalloc", "gdn_prefill_flags",
                     "gdn_prefill_gated",
                     "gdn_decode", "gdn_decode_flags", "gdn_output_gate", "gdn_device_status",
                     "gdn_last_error", "gdn_version")
@@ -79,6 +79,8 @@ def load() -> ctypes.CDLL:
         lib.gdn_prefill_noalloc.restype = i32
         lib.gdn_prefill_resolve.argtypes = [i64, i64, i32]
         lib.gdn_prefill_resolve.restype = i32
+        lib.gdn_prefill_tc_launches.argtypes = [i64, i32, i32, i32]
+        lib.gdn_prefill_tc_launches.restype = i32
         lib.gdn_prefill_workspace_size.argtypes = [i64, i64, i32]
         lib.gdn_prefill_workspace_size.restype = ctypes.c_size_t
         lib.gdn_decode.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i64, i32, i32, i32, f32,

@@ -324,6 +324,12 @@ int gdn_output_gate(void *output, const void *gate, const void *weight, int weig
                        "gdn_output_gate launch");
 }
 
+int gdn_prefill_tc_launches(int64_t num_seqs, int num_qk_heads, int num_v_heads, int num_sms) {
+    if (num_seqs <= 0 || num_qk_heads <= 0 || num_v_heads <= 0 || num_v_heads % num_qk_heads != 0) return 0;
+    const int nh = ((num_v_heads / num_qk_heads) % 2 == 0) ? 2 : 1;
+    return gdn::prefill_tc_overlap_tail(num_seqs * num_v_heads, num_sms, nh) > 0 ? 4 : 2;
+}
+
 int gdn_prefill_resolve(int64_t total_tokens, int64_t num_seqs, int method) {
     gdn::PrefillArgs p{};
     p.total_tokens = total_tokens;

@@ -62,6 +62,10 @@ bool prefill_chunked_supported(const PrefillArgs &p);
 // short group's chains run while the rest is being prepped (fork and join through
 // events; same kernels, same results).
 cudaError_t launch_prefill_tc(const PrefillArgs &p, void *workspace, cudaStream_t stream, bool overlap = false);
+// Chains launch_prefill_tc puts on the overlap stream for `chains` chains on `sms` SMs
+// (0: no split): chains mod sms when there are more chains than SMs and that tail is a
+// whole number of prep CTAs (heads_per_prep_cta v-heads each).
+int64_t prefill_tc_overlap_tail(int64_t chains, int sms, int heads_per_prep_cta);
 bool prefill_tc_supported(const PrefillArgs &p);
 size_t prefill_tc_workspace_bytes(const PrefillArgs &p);
 // Prep of the chains (sequence-major (sequence, v-head) indices) [chain_begin, chain_end)

@@ -636,6 +636,12 @@ size_t prefill_tc_workspace_bytes(const PrefillArgs &p) {
     return static_cast<size_t>(tc_workspace_bytes(p.total_tokens, p.num_seqs, p.Hv));
 }
 
+int64_t prefill_tc_overlap_tail(int64_t chains, int sms, int heads_per_prep_cta) {
+    if (sms <= 0 || chains <= sms) return 0;
+    const int64_t tail = chains % sms;
+    return (tail > 0 && tail % heads_per_prep_cta == 0) ? tail : 0;
+}
+
 namespace {
 
 // The library's second stream of a device (highest priority) and its fork / join events,
@@ -718,9 +724,9 @@ cudaError_t launch_prefill_tc(const PrefillArgs &p, void *workspace, cudaStream_
     if (overlap) {
         std::lock_guard<std::mutex> lock(g_overlap_mu);
         OverlapStream *o = overlap_stream(stream);
-        if (o && ctas > o->sms) {
-            const int64_t tail = ctas % o->sms;
-            if (tail > 0 && tail % prep_heads_per_cta(p) == 0) {
+        if (o) {
+            const int64_t tail = prefill_tc_overlap_tail(ctas, o->sms, prep_heads_per_cta(p));
+            if (tail > 0) {
                 if ((e = cudaEventRecord(o->fork, stream)) != cudaSuccess) return e;
                 if ((e = cudaStreamWaitEvent(o->aux, o->fork, 0)) != cudaSuccess) return e;
                 if ((e = launch_range(ctas - tail, ctas, o->aux)) != cudaSuccess) return e;

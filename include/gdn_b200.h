@@ -185,6 +185,14 @@ GDN_API int gdn_prefill_gated(const void *q, const void *k, const void *v, const
  * reference. */
 GDN_API int gdn_prefill_resolve(int64_t total_tokens, int64_t num_seqs, int method);
 
+/* Kernel launches of one tcgen05 prefill through the pooled-workspace entry points
+ * (gdn_prefill, gdn_prefill_ex, gdn_prefill_flags, gdn_prefill_gated without its gating
+ * pass) on a device with `num_sms` SMs: 2 (chunk prep, chains), or 4 when the last
+ * partial wave of (sequence, v-head) chains is split onto the library's second stream
+ * (more chains than SMs, chains mod SMs > 0 and a whole number of prep CTAs); 0 for
+ * invalid shapes.  Host arithmetic only.  No counterpart in the reference. */
+GDN_API int gdn_prefill_tc_launches(int64_t num_seqs, int num_qk_heads, int num_v_heads, int num_sms);
+
 /* Workspace bytes gdn_prefill_ws needs for GDN_PREFILL_TCGEN05:
  * (ceil(total_tokens / 64) + num_seqs) * num_v_heads * 41984.  No counterpart in the reference. */
 GDN_API size_t gdn_prefill_workspace_size(int64_t num_seqs, int64_t total_tokens, int num_v_heads);

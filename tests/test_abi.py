@@ -102,3 +102,16 @@ def test_error_maps_to_python_exceptions():
         _lib.check(_decode(lib, D=64))
     with pytest.raises(ValueError):
         _lib.check(_decode(lib, q=None))
+
+
+@pytest.mark.parametrize("n,hq,hv,sms,launches", [
+    (16, 16, 32, 148, 4),    # 512 chains: the last 68 go to the second stream
+    (4, 16, 32, 148, 2),     # fewer chains than SMs
+    (37, 2, 4, 148, 2),      # 148 chains: whole waves, no split
+    (13, 4, 12, 148, 4),     # one v-head per prep CTA: tail of 8
+    (16, 16, 32, 147, 2),    # a tail of 71 is not a whole number of two-head prep CTAs
+    (1, 3, 4, 148, 0),       # invalid head counts
+])
+def test_prefill_tc_launch_count_rule(n, hq, hv, sms, launches):
+    """The host query of the tcgen05 prefill's launch count (the wave-split rule)."""
+    assert _lib.load().gdn_prefill_tc_launches(n, hq, hv, sms) == launches
