@@ -297,3 +297,24 @@ def test_prefill_tc_wave_split_under_graph_capture():
     fk.device_status()
     assert torch.equal(og, o) and torch.equal(sg, s)
     del graph
+
+
+@pytest.mark.parametrize("n_seqs", [3, 16])
+def test_prefill_tc_launch_count_matches_query(n_seqs):
+    """The kernels one pooled tcgen05 call launches (counted by the profiler) are what
+    gdn_prefill_tc_launches reports: 2 below the wave-split threshold, 4 above it."""
+    from torch.profiler import ProfilerActivity, profile
+    from fastaf_kernel_b200 import _lib
+    x = W.prefill_inputs([128] * n_seqs, seed=35)
+    g = _gpu(x)
+    run = lambda: fk.kernel(g["q"], g["k"], g["v"], g["state"], g["A_log"], g["a"], g["dt_bias"], g["b"],
+                            g["cu_seqlens"], g["scale"], method="tcgen05", validate=False)
+    run()
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        run()
+        torch.cuda.synchronize()
+    names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+    ours = [n for n in names if "chunk_prep_kernel" in n or "prefill_tc_kernel" in n]
+    sms = torch.cuda.get_device_properties(DEV).multi_processor_count
+    assert len(ours) == _lib.load().gdn_prefill_tc_launches(n_seqs, 16, 32, sms), names
