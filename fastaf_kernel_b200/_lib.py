@@ -34,7 +34,7 @@ EXPORTED_SYMBOLS = ("gdn_prefill", "gdn_prefill_ex", "gdn_prefill_ws", "gdn_pref
                     "gdn_prefill_resolve", "gdn_prefill_tc_launches", "gdn_prefill_noalloc", "gdn_prefill_flags",
                     "gdn_prefill_gated",
                     "gdn_decode", "gdn_decode_flags", "gdn_output_gate", "gdn_device_status",
-                    "gdn_last_error", "gdn_version")
+                    "gdn_set_wait_limit_ns", "gdn_last_error", "gdn_version")
 
 _lock = threading.Lock()
 _lib = None
@@ -97,6 +97,8 @@ def load() -> ctypes.CDLL:
         lib.gdn_output_gate.restype = i32
         lib.gdn_device_status.argtypes = [vp]
         lib.gdn_device_status.restype = i32
+        lib.gdn_set_wait_limit_ns.argtypes = [ctypes.c_uint64]
+        lib.gdn_set_wait_limit_ns.restype = ctypes.c_uint64
         lib.gdn_last_error.argtypes = []
         lib.gdn_last_error.restype = ctypes.c_char_p
         lib.gdn_version.argtypes = []

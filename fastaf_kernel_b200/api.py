@@ -120,8 +120,11 @@ def kernel(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: Optional[to
     cast to int32 as the reference does, :458).  Returns
     (output [T, Hv, D] bf16, new_state [N, Hv, D, D] fp32).
 
-    ``validate`` checks cu_seqlens on the host (start 0, end T, non-decreasing);
-    for a device-resident cu_seqlens that costs one device-to-host copy.
+    cu_seqlens must start at 0, end at T and never decrease.  A host (CPU) cu_seqlens
+    is checked here when ``validate`` is true (the default); a device-resident one is
+    checked by the kernels themselves, so a call never synchronizes with the device to
+    check it: the kernels clamp bad entries (no out-of-bounds access) and record the
+    error, which ``device_status()`` raises as ValueError.
     """
     device = q.device
     for name, t in (("q", q), ("k", k), ("v", v), ("A_log", A_log), ("a", a),
@@ -144,8 +147,8 @@ def kernel(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: Optional[to
     N = cu_seqlens.shape[0] - 1
     if N < 0:
         raise ValueError("cu_seqlens must have at least one entry")
-    if validate:
-        _check_cu_seqlens_host(cu_seqlens.detach().to("cpu", torch.int64), T)
+    if validate and not cu_seqlens.is_cuda:
+        _check_cu_seqlens_host(cu_seqlens.detach().to(torch.int64), T)
     cu = cu_seqlens.to(device=device, dtype=torch.int32).contiguous()
     scale = _scale(scale, D)
 
@@ -372,8 +375,10 @@ def kernel_decode_dps(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_s
 
 
 def device_status(device: Optional[torch.device] = None) -> None:
-    """Synchronize the current stream and raise if a kernel timed out on a
-    bounded device-side wait since the last check (the flag is then cleared)."""
+    """Synchronize the current stream and raise what the kernels recorded on the device
+    since the last check (the record is then cleared): ``GdnError`` (status
+    GDN_ERR_DEVICE_TIMEOUT) if a tcgen05 prefill CTA gave up on a bounded device-side
+    wait, ``ValueError`` if a prefill read a malformed device-resident cu_seqlens."""
     device = device or torch.device("cuda", torch.cuda.current_device())
     with torch.cuda.device(device):
         _lib.check(_lib.load().gdn_device_status(torch.cuda.current_stream(device).cuda_stream))

@@ -109,12 +109,19 @@ const char *gdn_version(void) { return "gdn_b200 0.1.0 sm_100a"; }
 int gdn_device_status(void *stream) {
     g_last_error[0] = '\0';
     int code = 0;
-    const cudaError_t e = gdn::read_tc_device_error(static_cast<cudaStream_t>(stream), &code, true);
+    const cudaError_t e = gdn::read_device_status(static_cast<cudaStream_t>(stream), &code, true);
     if (e != cudaSuccess) return cuda_status(e, "gdn_device_status");
+    if (code == gdn::kErrCuSeqlens)
+        return fail(GDN_ERR_INVALID_ARGUMENT,
+                    "cu_seqlens was not an offsets array over [0, total_tokens] (an entry out of range, "
+                    "a decreasing pair, or a first entry != 0 / last entry != total_tokens); the kernels "
+                    "clamped it, the results of the affected sequences are meaningless");
     if (code != 0)
         return fail(GDN_ERR_DEVICE_TIMEOUT, "a prefill CTA timed out waiting at site %d", code);
     return GDN_OK;
 }
+
+uint64_t gdn_set_wait_limit_ns(uint64_t ns) { return gdn::set_wait_limit_ns(ns); }
 
 int gdn_decode(const void *q, const void *k, const void *v, const float *state,
                const void *A_log, const void *a, const void *dt_bias, const void *b,
@@ -198,6 +205,7 @@ static int prefill_impl(const void *q, const void *k, const void *v, const float
     p.norm_w = norm_w;
     p.norm_w_dtype = norm_w_dtype;
     p.norm_eps = norm_eps;
+    p.status = gdn::device_status_word();
     const auto s = static_cast<cudaStream_t>(stream);
     if (flags & GDN_FLAG_QK_L2NORM) {
         // Normalised q and k into pool scratch, then the prefill on them.

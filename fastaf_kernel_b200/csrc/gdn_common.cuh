@@ -28,6 +28,23 @@ __device__ __forceinline__ float log_decay(float exp_A_log, float a, float dt_bi
     return -exp_A_log * softplus_torch(a + dt_bias);
 }
 
+// Code a prefill kernel records in the library's device status word (read and cleared
+// by gdn_device_status) when cu_seqlens is not an offsets array over [0, T]: an entry
+// outside [0, T], a decreasing pair, cu_seqlens[0] != 0 or cu_seqlens[N] != T.  The
+// kernels clamp such entries, so nothing is read or written out of bounds; the results
+// of the affected sequences are then meaningless.  (Bounded-wait give-ups record their
+// site, 1..99, in the same word.)
+constexpr int kErrCuSeqlens = 100;
+
+// Called by one thread of each CTA that processes sequence n of N: the raw bounds of
+// sequence n against the offsets contract (first error kept).
+__device__ __forceinline__ void check_seq_bounds(const int32_t *cu, int64_t n, int64_t N, int64_t T, int *status) {
+    if (status == nullptr) return;
+    const int64_t s0 = cu[n], s1 = cu[n + 1];
+    if (s0 < 0 || s1 > T || s1 < s0 || (n == 0 && s0 != 0) || (n == N - 1 && s1 != T))
+        atomicCAS(status, 0, kErrCuSeqlens);
+}
+
 // beta = sigmoid(b)  (solution/gdn_baseline_torch.py:44)
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
 

@@ -38,6 +38,9 @@ struct PrefillArgs {
     const void *norm_w = nullptr;
     int norm_w_dtype = 0;
     float norm_eps = 0.0f;
+    // The device status word on this device (device_status_word()), where the kernels
+    // record a malformed cu_seqlens; nullptr: no check.
+    int *status = nullptr;
 };
 
 // Set the message gdn_last_error() returns on this thread.
@@ -73,7 +76,14 @@ size_t prefill_tc_workspace_bytes(const PrefillArgs &p);
 cudaError_t launch_chunk_prep(const PrefillArgs &p, uint8_t *ws_T, __nv_bfloat16 *ws_P, float *ws_g,
                               cudaStream_t stream, int64_t chain_begin = 0, int64_t chain_end = -1);
 int prep_heads_per_cta(const PrefillArgs &p);
-// Site of the first bounded device wait of the tcgen05 prefill that gave up (0 = none).
-cudaError_t read_tc_device_error(cudaStream_t stream, int *code, bool clear);
+// The device status word: 0, the site (1..99) of a bounded device wait of the tcgen05
+// prefill that gave up, or kErrCuSeqlens.  read_device_status synchronizes `stream`.
+cudaError_t read_device_status(cudaStream_t stream, int *code, bool clear);
+// Its device address on the current device (looked up on every call, so it follows a
+// new primary context), or nullptr when the lookup fails.
+int *device_status_word();
+// Limit of every bounded device wait of the tcgen05 chains, in ns (0: the default 2 s);
+// returns the previous setting.
+uint64_t set_wait_limit_ns(uint64_t ns);
 
 }  // namespace gdn

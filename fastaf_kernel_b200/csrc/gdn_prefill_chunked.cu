@@ -77,6 +77,8 @@ struct ChunkParams {
     int gate_dtype, param_dtype;
     __nv_bfloat16 *out;
     float *new_state;
+    int64_t num_seqs;
+    int *status;     // device status word (malformed cu_seqlens), or nullptr
 };
 
 // Issue the cp.async copies of chunk tokens [t0, t0+64) into stage `st`.
@@ -106,6 +108,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_chunked_mma_kernel(const 
     const int64_t n = chain / p.Hv;
     const int h = static_cast<int>(chain % p.Hv);
     const int hq = h / (p.Hv / p.Hq);
+    if (tid == 0 && h == 0) check_seq_bounds(p.cu_seqlens, n, p.num_seqs, p.T, p.status);
     int64_t s0 = p.cu_seqlens[n], s1 = p.cu_seqlens[n + 1];
     s0 = s0 < 0 ? 0 : (s0 > p.T ? p.T : s0);
     s1 = s1 < s0 ? s0 : (s1 > p.T ? p.T : s1);
@@ -468,7 +471,7 @@ cudaError_t launch_prefill_chunked(const PrefillArgs &p, cudaStream_t stream) {
     ChunkParams cp{static_cast<const __nv_bfloat16 *>(p.q), static_cast<const __nv_bfloat16 *>(p.k),
                    static_cast<const __nv_bfloat16 *>(p.v), p.state, p.A_log, p.a, p.dt_bias, p.b,
                    p.cu_seqlens, p.total_tokens, p.Hq, p.Hv, p.scale, p.gate_dtype, p.param_dtype,
-                   static_cast<__nv_bfloat16 *>(p.out), p.new_state};
+                   static_cast<__nv_bfloat16 *>(p.out), p.new_state, p.num_seqs, p.status};
     prefill_chunked_mma_kernel<<<static_cast<unsigned>(ctas), kThreads, SMEM_BYTES, stream>>>(cp);
     return cudaGetLastError();
 }

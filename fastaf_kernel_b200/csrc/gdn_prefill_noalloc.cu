@@ -32,9 +32,12 @@ constexpr size_t kNoAllocWorkspaceBytes = size_t(64) << 20;
 
 static __device__ __align__(256) unsigned char g_noalloc_ws[kNoAllocWorkspaceBytes];
 
-// Device address of g_noalloc_ws on the current device, resolved once per device
-// (cudaGetSymbolAddress with that device current) and cached.
-cudaError_t noalloc_workspace(void **ptr) {
+// Device address of g_noalloc_ws on the current device.  Outside a stream capture it is
+// looked up on every call (cudaGetSymbolAddress with that device current: a table lookup
+// once the module is loaded), so it follows a new primary context after a device reset;
+// inside a capture the last address seen on this device is used, since loading the module
+// there is not allowed -- so the device's first call must come before any capture.
+cudaError_t noalloc_workspace(void **ptr, cudaStream_t stream) {
     constexpr int kMaxDevices = 64;
     static std::mutex mu;
     static void *addr[kMaxDevices] = {};
@@ -42,8 +45,11 @@ cudaError_t noalloc_workspace(void **ptr) {
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    e = cudaStreamIsCapturing(stream, &cs);
+    if (e != cudaSuccess) return e;
     std::lock_guard<std::mutex> lock(mu);
-    if (addr[dev] == nullptr) {
+    if (cs == cudaStreamCaptureStatusNone || addr[dev] == nullptr) {
         void *p = nullptr;
         e = cudaGetSymbolAddress(&p, g_noalloc_ws);
         if (e != cudaSuccess) return e;
@@ -79,7 +85,7 @@ int gdn_prefill_noalloc(const void *q, const void *k, const void *v, const float
         return GDN_ERR_INVALID_ARGUMENT;
     }
     void *ws = nullptr;
-    const cudaError_t e = noalloc_workspace(&ws);
+    const cudaError_t e = noalloc_workspace(&ws, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) {
         std::snprintf(msg, sizeof(msg), "gdn_prefill_noalloc: workspace address: %s", cudaGetErrorString(e));
         gdn::set_last_error(msg);

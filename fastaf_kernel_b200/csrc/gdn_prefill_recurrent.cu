@@ -65,9 +65,9 @@ __global__ void __launch_bounds__(kRecThreads)
 prefill_recurrent_kernel(const __nv_bfloat16 *__restrict__ q, const __nv_bfloat16 *__restrict__ k,
                          const __nv_bfloat16 *__restrict__ v, const float *__restrict__ state,
                          const void *A_log, const void *a, const void *dt_bias, const void *b,
-                         const int32_t *__restrict__ cu_seqlens, int64_t T, int Hq, int Hv,
+                         const int32_t *__restrict__ cu_seqlens, int64_t N, int64_t T, int Hq, int Hv,
                          float scale, int gate_dtype, int param_dtype,
-                         __nv_bfloat16 *__restrict__ out, float *__restrict__ new_state) {
+                         __nv_bfloat16 *__restrict__ out, float *__restrict__ new_state, int *status) {
     __shared__ __align__(16) float k_s[kTokBlock][2][kHalfPad];
     __shared__ __align__(16) float q_s[kTokBlock][2][kHalfPad];
     __shared__ float v_s[kTokBlock][kRecRows];
@@ -83,6 +83,7 @@ prefill_recurrent_kernel(const __nv_bfloat16 *__restrict__ q, const __nv_bfloat1
     const int row_base = slab * kRecRows;
     const int row = row_base + (tid >> 1);
 
+    if (tid == 0 && blockIdx.x % (2 * Hv) == 0) check_seq_bounds(cu_seqlens, n, N, T, status);
     int64_t s0 = cu_seqlens[n], s1 = cu_seqlens[n + 1];
     s0 = s0 < 0 ? 0 : (s0 > T ? T : s0);
     s1 = s1 < s0 ? s0 : (s1 > T ? T : s1);
@@ -184,8 +185,8 @@ cudaError_t launch_prefill_recurrent(const PrefillArgs &p, cudaStream_t stream) 
     prefill_recurrent_kernel<<<static_cast<unsigned>(ctas), kRecThreads, 0, stream>>>(
         static_cast<const __nv_bfloat16 *>(p.q), static_cast<const __nv_bfloat16 *>(p.k),
         static_cast<const __nv_bfloat16 *>(p.v), p.state, p.A_log, p.a, p.dt_bias, p.b,
-        p.cu_seqlens, p.total_tokens, p.Hq, p.Hv, p.scale, p.gate_dtype, p.param_dtype,
-        static_cast<__nv_bfloat16 *>(p.out), p.new_state);
+        p.cu_seqlens, p.num_seqs, p.total_tokens, p.Hq, p.Hv, p.scale, p.gate_dtype, p.param_dtype,
+        static_cast<__nv_bfloat16 *>(p.out), p.new_state, p.status);
     return cudaGetLastError();
 }
 

@@ -34,11 +34,14 @@
 // The fp32 state lives in TMEM columns [0,128) for the whole sequence.  The barrier
 // protocol is modelled on the CPU under random schedules (tests/test_tc_chain_protocol.py).
 //
-// Every wait is bounded (about 2 s).  A wait that gives up records its site in
-// g_tc_error and raises a shared abort flag; every role then stops at its next wait,
-// the issuing thread waits (bounded) for its MMAs and copies still in flight, and
-// the CTA frees TMEM and exits.
+// Every wait is bounded (2 s by default, TcParams::wait_ns).  A wait that gives up
+// records its site in g_tc_error and raises a shared abort flag; every role then stops
+// at its next wait (the prep warps' staging hand-off included: it is an mbarrier, not a
+// named barrier, so a warp that stopped cannot leave the others waiting), the issuing
+// thread waits for the last commit of every MMA batch it issued and the copy thread for
+// every copy it issued (both bounded by kDrainWaitNs), and the CTA frees TMEM and exits.
 #include <cuda_bf16.h>
+#include <atomic>
 #include <cstring>
 #include <mutex>
 
@@ -52,6 +55,9 @@
 namespace gdn {
 
 __device__ int g_tc_error = 0;
+
+// Limit of a role's wait when the caller sets none (gdn_set_wait_limit_ns(0)).
+constexpr uint64_t kDefaultWaitNs = 2000000000ull;
 
 namespace {
 
@@ -97,11 +103,15 @@ constexpr uint32_t TM_O = 448;    // [448,512) (Gamma Q S_hi^T)^T, then O^T (zer
 
 enum WaitSite { kWaitTma = 1, kWaitWU = 3, kWaitD = 4, kWaitS = 5, kWaitTT = 6,
                 kWaitW = 7, kWaitSS = 8, kWaitDS = 9, kWaitT = 10, kWaitIssue = 11, kWaitUD = 12 };
+// Limit of the waits for the CTA's own MMAs and copies in flight once it stops (these
+// complete on their own; the limit only keeps a broken device from holding the SM).
+constexpr uint64_t kDrainWaitNs = 2000000000ull;
 // (output reads O^T of chunk c before the delta batch of chunk c + 1 overwrites it)
 
 struct TcParams {
     const float *state;
     const int32_t *cu_seqlens;
+    int64_t num_seqs;
     int64_t T;
     int Hq, Hv;
     float scale;
@@ -111,10 +121,11 @@ struct TcParams {
     const float *ws_g;
     const __nv_bfloat16 *ws_P;
     int64_t chain0;   // (sequence, v-head) chain of blockIdx.x = 0
+    uint64_t wait_ns; // limit of every role's wait (ns)
 };
 
 struct Bars {
-    uint64_t tma[2], wdone, udone, d, s, qs, w, ss, ds, tw, tu, free_[2], oread;
+    uint64_t tma[2], wdone, udone, d, s, qs, w, ss, ds, tw, tu, free_[2], oread, stg;
 };
 
 __device__ __forceinline__ void issue_chunk(const CUtensorMap *qmap, const CUtensorMap *kmap,
@@ -134,14 +145,15 @@ __device__ __forceinline__ void issue_chunk(const CUtensorMap *qmap, const CUten
 }
 
 // Bounded wait that gives up at once when another role has already given up.
-__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, int site, volatile int *abort) {
+__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, int site, volatile int *abort,
+                                             uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 63u) == 0) {
             if (*abort) return false;
-            if (global_timer_ns() - t0 > 2000000000ull) {
+            if (global_timer_ns() - t0 > limit_ns) {
                 atomicExch(&g_tc_error, site);
                 *abort = 1;
                 return false;
@@ -149,9 +161,16 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, int 
         }
     }
 }
+// Wait for this CTA's own asynchronous work (an MMA commit or a copy it issued), also
+// after a give-up: it completes on its own.
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int site) {
+    volatile int never = 0;
+    wait_bounded(bar, parity, site, &never, kDrainWaitNs);
+}
 // Whole-warp wait: reconverges the warp for the next .aligned tcgen05 op.
-__device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, int site, volatile int *abort) {
-    const bool ok = wait_bounded(bar, parity, site, abort);
+__device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, int site, volatile int *abort,
+                                          uint64_t limit_ns) {
+    const bool ok = wait_bounded(bar, parity, site, abort, limit_ns);
     __syncwarp();
     tc_fence_after();
     return __all_sync(0xffffffffu, ok);
@@ -160,9 +179,6 @@ __device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, int sit
 __device__ __forceinline__ void warp_arrive(uint32_t bar, int lane) {
     __syncwarp();
     if (lane == 0) mbar_arrive(bar);
-}
-__device__ __forceinline__ void named_sync(int id, int nthreads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -182,6 +198,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
     const int64_t n = chain / p.Hv;
     const int h = static_cast<int>(chain % p.Hv);
     const int hq = h / (p.Hv / p.Hq);
+    if (tid == 0 && h == 0) check_seq_bounds(p.cu_seqlens, n, p.num_seqs, p.T, &g_tc_error);
     int64_t s0 = p.cu_seqlens[n], s1 = p.cu_seqlens[n + 1];
     s0 = s0 < 0 ? 0 : (s0 > p.T ? p.T : s0);
     s1 = s1 < s0 ? s0 : (s1 > p.T ? p.T : s1);
@@ -196,6 +213,9 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
     // free[b]: chunk c's S-update batch (the last reader of stage c & 1 and P buffer c & 1) is done
     const uint32_t b_free0 = smem_u32(&bars.free_[0]), b_free1 = smem_u32(&bars.free_[1]);
     const uint32_t b_oread = smem_u32(&bars.oread);   // the prep warps have read O^T of a chunk
+    // the four prep warps' hand-offs around the output staging tile (two per output chunk)
+    const uint32_t b_stg = smem_u32(&bars.stg);
+    const uint64_t wl = p.wait_ns;
     float *dst_state = p.new_state + chain * kHeadDim * kHeadDim;
 
     if (warp == 0) {
@@ -215,6 +235,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             mbar_init(b_free0, 1);
             mbar_init(b_free1, 1);
             mbar_init(b_oread, 4);
+            mbar_init(b_stg, 4);
             abort_flag = 0;
             fence_mbar_init();
         }
@@ -334,7 +355,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                         t_idle = global_timer_ns();
                     } else if (*abort) {
                         ok = false;
-                    } else if (global_timer_ns() - t_idle > 2000000000ull) {
+                    } else if (global_timer_ns() - t_idle > wl) {
                         atomicExch(&g_tc_error, kWaitIssue);
                         *abort = 1;
                         ok = false;
@@ -343,13 +364,12 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             }
             // Wait (bounded, also after a give-up) for the last commit of every kind, so
             // no MMA or barrier arrive is still in flight when the CTA leaves.
-            volatile int never = 0;
-            if (n6w) wait_bounded(b_wdone, (n6w - 1) & 1, kWaitWU, &never);
-            if (n6u) wait_bounded(b_udone, (n6u - 1) & 1, kWaitUD, &never);
-            if (n8) wait_bounded(b_d, (n8 - 1) & 1, kWaitD, &never);
-            if (n10) wait_bounded(b_s, (n10 - 1) & 1, kWaitS, &never);
+            if (n6w) drain_wait(b_wdone, (n6w - 1) & 1, kWaitWU);
+            if (n6u) drain_wait(b_udone, (n6u - 1) & 1, kWaitUD);
+            if (n8) drain_wait(b_d, (n8 - 1) & 1, kWaitD);
+            if (n10) drain_wait(b_s, (n10 - 1) & 1, kWaitS);
             for (int c = n10 > 2 ? n10 - 2 : 0; c < n10; ++c)
-                wait_bounded((c & 1) ? b_free1 : b_free0, (c >> 1) & 1, kWaitS, &never);
+                drain_wait((c & 1) ? b_free1 : b_free0, (c >> 1) & 1, kWaitS);
         }
         __syncwarp();
     } else if (warp == 13) {
@@ -359,39 +379,52 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         // c - 2 is done, the T' tiles once the U^T batch of c - 1 is done.
         if (lane == 0) {
             int issued = 0, n_tw = 0, n_tu = 0;
-            bool ok = true;
             auto unit_of = [&](int c) { return tc_slot(s0, c, n) * p.Hv + h; };
             for (int c = 0; c < nch; ++c) {
                 const int64_t unit = unit_of(c);
-                if (c >= 1 && !(ok = wait_bounded(b_wdone, (c - 1) & 1, kWaitWU, abort))) break;
+                if (c >= 1 && !wait_bounded(b_wdone, (c - 1) & 1, kWaitWU, abort, wl)) break;
                 mbar_arrive_expect_tx(b_tw, 2 * kTcTileBytes);
                 bulk_load(sbase + OFF_T2H, p.ws_T + unit * kTcTBytes + 2 * kTcTileBytes, 2 * kTcTileBytes, b_tw);
                 ++n_tw;
-                if (c >= 2 && !(ok = wait_bounded((c & 1) ? b_free1 : b_free0, ((c - 2) >> 1) & 1, kWaitS, abort)))
+                if (c >= 2 && !wait_bounded((c & 1) ? b_free1 : b_free0, ((c - 2) >> 1) & 1, kWaitS, abort, wl))
                     break;
                 issue_chunk(&qmap, &kmap, &vmap, sbase, c & 1, p.ws_P + unit * (kTcPBytes / 2),
                             p.ws_g + unit * (kTcGateBytes / 4), (c & 1) ? b_tma1 : b_tma0,
                             static_cast<int>(s0 + c * kC), hq, h);
                 ++issued;
-                if (c >= 1 && !(ok = wait_bounded(b_udone, (c - 1) & 1, kWaitUD, abort))) break;
+                if (c >= 1 && !wait_bounded(b_udone, (c - 1) & 1, kWaitUD, abort, wl)) break;
                 mbar_arrive_expect_tx(b_tu, 2 * kTcTileBytes);
                 bulk_load(sbase + OFF_T1H, p.ws_T + unit * kTcTBytes, 2 * kTcTileBytes, b_tu);
                 ++n_tu;
             }
-            if (!ok) {
-                // Give up: wait (bounded) for the copies still in flight.
-                volatile int never = 0;
-                for (int cc = issued > 2 ? issued - 2 : 0; cc < issued; ++cc)
-                    wait_bounded((cc & 1) ? b_tma1 : b_tma0, (cc >> 1) & 1, kWaitTma, &never);
-                if (n_tw) wait_bounded(b_tw, (n_tw - 1) & 1, kWaitT, &never);
-                if (n_tu) wait_bounded(b_tu, (n_tu - 1) & 1, kWaitT, &never);
-            }
+            // Wait for the copies still in flight (none after a normal run, where their
+            // readers have waited for them; after a give-up of any role, possibly some).
+            for (int cc = issued > 2 ? issued - 2 : 0; cc < issued; ++cc)
+                drain_wait((cc & 1) ? b_tma1 : b_tma0, (cc >> 1) & 1, kWaitTma);
+            if (n_tw) drain_wait(b_tw, (n_tw - 1) & 1, kWaitT);
+            if (n_tu) drain_wait(b_tu, (n_tu - 1) & 1, kWaitT);
         }
         __syncwarp();
     } else if (warp <= 4) {
         // ------------------------------------------------------------ prep (chunk c + 1 while c runs)
         const int pt = tid - 32;    // 0..127
-        auto write_out = [&](int c) {
+        // Hand-off among the four prep warps around the staging tile: completion 2j of
+        // b_stg (parity 0) = the rows of the previous output chunk have left it, 2j + 1
+        // (parity 1) = output chunk j is in it.  False: another role gave up.  (No timer
+        // of its own: it only waits for the other three prep warps, and each of their
+        // waits is bounded and raises the flag when it gives up.)
+        auto stage_sync = [&](uint32_t parity) {
+            warp_arrive(b_stg, lane);
+            bool ok = true;
+            while (!mbar_try_wait(b_stg, parity)) {
+                if (*abort) {
+                    ok = false;
+                    break;
+                }
+            }
+            return __all_sync(0xffffffffu, ok);
+        };
+        auto write_out = [&](int c) -> bool {
             uint32_t o[64];
             tmem_ld32(tmem_addr(tm, lane_base, TM_O), *reinterpret_cast<uint32_t(*)[32]>(o));
             tmem_ld32(tmem_addr(tm, lane_base, TM_O + 32), *reinterpret_cast<uint32_t(*)[32]>(o + 32));
@@ -407,7 +440,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             const int64_t t0 = s0 + static_cast<int64_t>(c) * kC;
             const int nt = static_cast<int>(s1 - t0 < kC ? s1 - t0 : kC);
             __nv_bfloat16 *so = reinterpret_cast<__nv_bfloat16 *>(sm + OFF_O);
-            named_sync(2, 128);   // the previous chunk's rows have left the staging tile
+            if (!stage_sync(0)) return false;   // the previous chunk's rows have left the staging tile
             // two tokens per packed conversion (the single-value one runs at a quarter of the
             // rate and these warps share their SMSPs with the state split)
             uint16_t *so16 = reinterpret_cast<uint16_t *>(so);
@@ -419,7 +452,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                 so16[ii * kHeadDim + row] = static_cast<uint16_t>(pk);
                 so16[(ii + 1) * kHeadDim + row] = static_cast<uint16_t>(pk >> 16);
             }
-            named_sync(2, 128);
+            if (!stage_sync(1)) return false;
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
                 const int idx = pt + 128 * u, i = idx >> 4, c16 = idx & 15;
@@ -427,13 +460,14 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                     *reinterpret_cast<uint4 *>(p.out + ((t0 + i) * p.Hv + h) * kHeadDim + c16 * 8) =
                         *reinterpret_cast<const uint4 *>(sm + OFF_O + i * 256 + c16 * 16);
             }
+            return true;
         };
         for (int c = 0; c < nch; ++c) {
             const int st = c & 1;
-            if (!wait_warp(st ? b_tma1 : b_tma0, (c >> 1) & 1, kWaitTma, abort)) break;
+            if (!wait_warp(st ? b_tma1 : b_tma0, (c >> 1) & 1, kWaitTma, abort, wl)) break;
             const float *g_Gam = reinterpret_cast<const float *>(sm + OFF_GST + st * kTcGateBytes) + 128;
             // diag(Gamma) Q once the previous chunk's Q S^T product has read the tile
-            if (c > 0 && !wait_warp(b_d, (c - 1) & 1, kWaitD, abort)) break;
+            if (c > 0 && !wait_warp(b_d, (c - 1) & 1, kWaitD, abort, wl)) break;
             {
                 // (diag(Gamma) Q)^T, MN-major [k][i]: thread pt = k reads column k of the Q
                 // tile (two threads per 4-byte word, conflict-free) and writes row k.
@@ -468,7 +502,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             tc_fence_before();
             warp_arrive(b_qs, lane);
             // -W as bf16 hi/lo, MN-major [k][i] (TMEM lane k holds row k of W^T)
-            if (!wait_warp(b_wdone, c & 1, kWaitWU, abort)) break;
+            if (!wait_warp(b_wdone, c & 1, kWaitWU, abort, wl)) break;
 #pragma unroll 1
             for (int hf = 0; hf < 2; ++hf) {
                 uint32_t r[32];
@@ -496,12 +530,10 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             warp_arrive(b_w, lane);
             // the previous chunk's output: O^T (TMEM lane v = column v of O) into registers,
             // release TM_O, then bf16 staging -> coalesced row stores
-            if (c > 0) {
-                if (!wait_warp(b_s, (c - 1) & 1, kWaitS, abort)) break;
-                write_out(c - 1);
-            }
+            if (c > 0 && (!wait_warp(b_s, (c - 1) & 1, kWaitS, abort, wl) || !write_out(c - 1))) break;
         }
-        if (nch > 0 && wait_warp(b_s, (nch - 1) & 1, kWaitS, abort)) write_out(nch - 1);
+        // (a warp leaves the loop early only after a give-up, which has raised the flag)
+        if (!*abort && nch > 0 && wait_warp(b_s, (nch - 1) & 1, kWaitS, abort, wl)) write_out(nch - 1);
     } else {
         // ------------------------------------------------------------ state path (chunk c)
         // Two halves of four warps (one per TMEM lane quadrant): half hs owns state
@@ -528,8 +560,8 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         for (int c = 0; c < nch; ++c) {
             const int st = c & 1;
             // the previous chunk's S update is done
-            if (c > 0 && !(ok = wait_warp(b_s, (c - 1) & 1, kWaitS, abort))) break;
-            if (!(ok = wait_warp(st ? b_tma1 : b_tma0, (c >> 1) & 1, kWaitTma, abort))) break;
+            if (c > 0 && !(ok = wait_warp(b_s, (c - 1) & 1, kWaitS, abort, wl))) break;
+            if (!(ok = wait_warp(st ? b_tma1 : b_tma0, (c >> 1) & 1, kWaitTma, abort, wl))) break;
             const float *g_beta = reinterpret_cast<const float *>(sm + OFF_GST + st * kTcGateBytes);
             const float *g_Gam = g_beta + 128, *g_dec = g_beta + 192;
             // S -> bf16 hi/lo (TMEM A operands of the delta and output products); S <- Gamma_63 S
@@ -560,7 +592,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             tc_fence_before();
             warp_arrive(b_ss, lane);
             // delta (fp32, TMEM) -> bf16 (output path) and exp(gamma_63 - gamma_i) delta -> hi/lo
-            if (!(ok = wait_warp(b_d, c & 1, kWaitD, abort))) break;
+            if (!(ok = wait_warp(b_d, c & 1, kWaitD, abort, wl))) break;
             {
                 uint32_t r[32], x[32], db[16], dh[16], dl[16];
                 tmem_ld32(tmem_addr(tm, lane_base, TM_U + 32 * hs), r);
@@ -586,7 +618,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             tc_fence_before();
             warp_arrive(b_ds, lane);
         }
-        if (ok && wait_warp(b_s, (nch - 1) & 1, kWaitS, abort)) {
+        if (ok && wait_warp(b_s, (nch - 1) & 1, kWaitS, abort, wl)) {
             float *dst = dst_state + v * kHeadDim;
 #pragma unroll 1
             for (int q4 = 2 * hs; q4 < 2 * hs + 2; ++q4) {
@@ -646,6 +678,9 @@ namespace {
 
 // The library's second stream of a device (highest priority) and its fork / join events,
 // created on first use and kept until exit; `mu` serialises the fork-join enqueue.
+// Limit of the chains' bounded waits set by gdn_set_wait_limit_ns (0: kDefaultWaitNs).
+std::atomic<uint64_t> g_wait_limit_ns{0};
+
 struct OverlapStream {
     cudaStream_t aux = nullptr;
     cudaEvent_t fork = nullptr, join = nullptr;
@@ -684,6 +719,24 @@ OverlapStream *overlap_stream(cudaStream_t stream) {
     return o.aux ? &o : nullptr;
 }
 
+// Whether this call may fork onto the shared overlap stream `aux`: either neither stream
+// is being captured, or `stream` is being captured (the fork then pulls `aux` into that
+// capture until it ends) and `aux` is free or already in that same capture.  While `aux`
+// belongs to one capture, calls on other streams -- eager ones, or ones captured into
+// another graph -- must not touch it: they run unsplit on their own stream.
+bool aux_usable(cudaStream_t stream, cudaStream_t aux) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone, ca = cudaStreamCaptureStatusNone;
+    unsigned long long id_s = 0, id_a = 0;
+    if (cudaStreamGetCaptureInfo(stream, &cs, &id_s) != cudaSuccess ||
+        cudaStreamGetCaptureInfo(aux, &ca, &id_a) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    if (cs == cudaStreamCaptureStatusInvalidated || ca == cudaStreamCaptureStatusInvalidated) return false;
+    if (ca == cudaStreamCaptureStatusNone) return true;
+    return cs == cudaStreamCaptureStatusActive && id_s == id_a;
+}
+
 }  // namespace
 
 // The prep and chain kernels of every chain on `stream`, or -- with `overlap`, more
@@ -712,19 +765,21 @@ cudaError_t launch_prefill_tc(const PrefillArgs &p, void *workspace, cudaStream_
         return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return e;
+    const uint64_t limit = g_wait_limit_ns.load(std::memory_order_relaxed);
+    const uint64_t wait_ns = limit ? limit : kDefaultWaitNs;
     // prep + chains of [c0, c1) on stream st
     auto launch_range = [&](int64_t c0, int64_t c1, cudaStream_t st) -> cudaError_t {
         cudaError_t er = launch_chunk_prep(p, ws_T, ws_P, ws_g, st, c0, c1);
         if (er != cudaSuccess) return er;
-        TcParams tp{p.state, p.cu_seqlens, p.total_tokens, p.Hq, p.Hv, p.scale,
-                    static_cast<__nv_bfloat16 *>(p.out), p.new_state, ws_T, ws_g, ws_P, c0};
+        TcParams tp{p.state, p.cu_seqlens, p.num_seqs, p.total_tokens, p.Hq, p.Hv, p.scale,
+                    static_cast<__nv_bfloat16 *>(p.out), p.new_state, ws_T, ws_g, ws_P, c0, wait_ns};
         prefill_tc_kernel<<<static_cast<unsigned>(c1 - c0), kThreads, SMEM_BYTES, st>>>(qm, km, vm, tp);
         return cudaGetLastError();
     };
     if (overlap) {
         std::lock_guard<std::mutex> lock(g_overlap_mu);
         OverlapStream *o = overlap_stream(stream);
-        if (o) {
+        if (o && aux_usable(stream, o->aux)) {
             const int64_t tail = prefill_tc_overlap_tail(ctas, o->sms, prep_heads_per_cta(p));
             if (tail > 0) {
                 if ((e = cudaEventRecord(o->fork, stream)) != cudaSuccess) return e;
@@ -739,7 +794,18 @@ cudaError_t launch_prefill_tc(const PrefillArgs &p, void *workspace, cudaStream_
     return launch_range(0, ctas, stream);
 }
 
-cudaError_t read_tc_device_error(cudaStream_t stream, int *code, bool clear) {
+uint64_t set_wait_limit_ns(uint64_t ns) { return g_wait_limit_ns.exchange(ns); }
+
+int *device_status_word() {
+    void *ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_tc_error) != cudaSuccess) {
+        cudaGetLastError();   // (not left pending for the caller's launch check)
+        return nullptr;
+    }
+    return static_cast<int *>(ptr);
+}
+
+cudaError_t read_device_status(cudaStream_t stream, int *code, bool clear) {
     cudaError_t e = cudaMemcpyFromSymbolAsync(code, g_tc_error, sizeof(int), 0,
                                               cudaMemcpyDeviceToHost, stream);
     if (e != cudaSuccess) return e;

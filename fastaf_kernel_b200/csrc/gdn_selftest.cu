@@ -248,8 +248,40 @@ selftest_roles_kernel(const __nv_bfloat16 *A, const __nv_bfloat16 *B, int N, int
     }
 }
 
+// Bounded wait on an mbarrier that nothing ever arrives on: the wait must give up after
+// `limit_ns` and return.  out[0] = 1 if the wait reported completion (a failure of the
+// check), out[1] = elapsed ns of the wait, out[2] = 1 when the kernel reached its end.
+__global__ void __launch_bounds__(32, 1) selftest_wait_timeout_kernel(uint64_t limit_ns,
+                                                                      unsigned long long *out) {
+    __shared__ uint64_t bar;
+    const uint32_t b = smem_u32(&bar);
+    if (threadIdx.x == 0) {
+        mbar_init(b, 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    if (threadIdx.x == 0) {
+        const uint64_t t0 = global_timer_ns();
+        const bool completed = mbar_wait(b, 0, limit_ns);
+        const uint64_t t1 = global_timer_ns();
+        out[0] = completed ? 1ull : 0ull;
+        out[1] = t1 - t0;
+        out[2] = 1ull;
+    }
+}
+
 }  // namespace
 }  // namespace gdn
+
+// Bounded-wait check: one warp waits on an mbarrier nobody arrives on, with a limit of
+// `limit_ns` (at most 0.1 s), and writes three counters to `out` (device, 3 x uint64).
+extern "C" __attribute__((visibility("default"))) int gdn_selftest_wait_timeout(uint64_t limit_ns, void *out,
+                                                                                void *stream) {
+    if (limit_ns == 0 || limit_ns > 100000000ull || out == nullptr) return -1;
+    gdn::selftest_wait_timeout_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+        limit_ns, static_cast<unsigned long long *>(out));
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
 
 extern "C" __attribute__((visibility("default"))) int gdn_selftest_umma(
     int mode, const void *A, const void *B, const void *X, int T, int H, int h, int N, int K,

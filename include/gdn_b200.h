@@ -75,8 +75,9 @@ extern "C" {
  *
  * Requirements: D == 128, Hv % Hq == 0, 16-byte aligned q/k/v/output/state
  * pointers.  cu_seqlens is read on the device; entries outside [0, T] or
- * decreasing are a caller error (the kernels clamp them so they never read or
- * write out of bounds).
+ * decreasing are a caller error, checked by the kernels themselves (no host
+ * synchronization): they clamp such entries so they never read or write out of
+ * bounds, and record the error for gdn_device_status().
  */
 GDN_API int gdn_prefill(const void *q, const void *k, const void *v, const float *state,
                 const void *A_log, const void *a, const void *dt_bias, const void *b,
@@ -232,13 +233,31 @@ GDN_API int gdn_decode_flags(const void *q, const void *k, const void *v, const 
                      float *new_state, int flags, void *stream);
 
 /*
- * Synchronizes `stream` and reports whether any chunked-prefill kernel since the
- * last call gave up on a bounded barrier wait (GDN_ERR_DEVICE_TIMEOUT; the flag
- * is cleared).  The kernels never spin unboundedly: a wait that times out
- * records its site here, drains its in-flight copies and exits.  No counterpart
- * in the reference (its Triton kernels have no device-side waits).
+ * Synchronizes `stream` and reports the library's device status word since the last
+ * call (the word is then cleared):
+ *   GDN_ERR_DEVICE_TIMEOUT    a tcgen05 prefill CTA gave up on a bounded barrier wait
+ *                             (the kernels never spin unboundedly: a wait that runs out
+ *                             records its site, the CTA waits for its own copies and MMAs
+ *                             in flight, frees its tensor memory and exits);
+ *   GDN_ERR_INVALID_ARGUMENT  a prefill read a cu_seqlens that is not an offsets array over
+ *                             [0, total_tokens] (checked on the device, where cu_seqlens
+ *                             lives, so a call never synchronizes to check it on the host;
+ *                             the kernels clamp such entries and never access memory out of
+ *                             bounds, but the affected sequences' results are meaningless).
+ * No counterpart in the reference (its Triton kernels have no device-side waits and
+ * its entry points do no validation).
  */
 GDN_API int gdn_device_status(void *stream);
+
+/*
+ * Limit, in nanoseconds, of every bounded device-side wait of the tcgen05 prefill
+ * chains launched after this call (process-wide; 0 restores the default of 2 s).
+ * Returns the previous setting (0 = default).  A serving process can lower it to
+ * detect a stalled kernel sooner; a limit below a chunk's normal latency makes
+ * healthy calls give up (gdn_device_status then reports GDN_ERR_DEVICE_TIMEOUT).
+ * No counterpart in the reference.
+ */
+GDN_API uint64_t gdn_set_wait_limit_ns(uint64_t ns);
 
 /* Message describing the calling thread's most recent failed call ("" if none). */
 GDN_API const char *gdn_last_error(void);

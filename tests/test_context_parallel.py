@@ -125,3 +125,21 @@ def test_segmented_prefill_gpu_equals_one_pass(method, P):
                                 x["b"], x["scale"], segments=P, method=method)
     fk.device_status()
     assert_parity(o.cpu(), ro.cpu(), s.cpu(), rs.cpu())
+
+
+@pytest.mark.gpu
+def test_segmented_prefill_gpu_against_oracle():
+    """8 segments of 4096 tokens of one sequence (Hq 16, Hv 32, nonzero initial state,
+    slow decay so the carried state matters) through the tcgen05 kernel, against the C
+    oracle over the whole 32768-token sequence, at the same tolerances as every prefill."""
+    import fastaf_kernel_b200 as fk
+    from oracle import c_oracle
+    dev = torch.device("cuda", 0)
+    x = W.prefill_inputs([8 * 4096], seed=64, decay_range=(0.99, 0.9999))
+    assert x["state"] is not None and float(x["state"].abs().max()) > 0
+    ro, rs = _whole(x, c_oracle.prefill)
+    g = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in x.items()}
+    o, s = cp.prefill_segmented(g["q"], g["k"], g["v"], g["state"], g["A_log"], g["a"], g["dt_bias"],
+                                g["b"], g["scale"], segments=8, method="tcgen05")
+    fk.device_status()
+    assert_parity(o.cpu(), ro, s.cpu(), rs)

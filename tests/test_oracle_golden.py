@@ -82,3 +82,23 @@ def test_decode_inplace_matches_out_of_place():
                                 inp["dt_bias"], inp["b"], inp["scale"], inplace=True)
     assert ns2.data_ptr() == st.data_ptr()
     assert torch.equal(out1, out2) and torch.equal(ns1, ns2)
+
+
+def test_reference_distribution_overflows_fp32_beyond_a_few_chunks():
+    """The reference test's input distribution (every input randn, so |k|^2 ~ 128 and
+    I - beta k k^T expands the state ~60-fold per token) overflows the fp32 recurrence
+    itself: the oracle's state is non-finite by 128 tokens.  No kernel can be held to the
+    oracle there; the tensor-core paths are held to keys whose recurrence stays bounded
+    (beta |k|^2 < 2), which tests/test_prefill_gpu.py covers at >= 256 tokens through auto."""
+    rng = np.random.Generator(np.random.PCG64(5))
+    T, Hq, Hv = 128, 4, 8
+    bf = lambda a: torch.from_numpy(a.astype(np.float32)).to(torch.bfloat16)
+    sn = rng.standard_normal
+    x = {"q": bf(sn((T, Hq, 128))), "k": bf(sn((T, Hq, 128))), "v": bf(sn((T, Hv, 128))),
+         "state": torch.from_numpy(sn((1, Hv, 128, 128)).astype(np.float32)),
+         "A_log": torch.from_numpy(sn(Hv).astype(np.float32)), "a": bf(sn((T, Hv))),
+         "dt_bias": torch.from_numpy(sn(Hv).astype(np.float32)), "b": bf(sn((T, Hv))),
+         "cu_seqlens": torch.tensor([0, T], dtype=torch.int32), "scale": 1.0 / np.sqrt(128)}
+    _, rs = c_oracle.prefill(x["q"], x["k"], x["v"], x["state"], x["A_log"], x["a"],
+                             x["dt_bias"], x["b"], x["cu_seqlens"], x["scale"])
+    assert not torch.isfinite(rs).all()

@@ -128,26 +128,54 @@ def test_prefill_gva_ratios(method):
         assert_parity(o.cpu(), ro, s.cpu(), rs)
 
 
-def test_chunked_equals_recurrent_long_prefill_sample():
-    """Full-size long-prefill shapes (16 x 8192, 32 heads): the three independent CUDA
-    kernels agree; the oracle checks sequence 0 over its first 2048 tokens."""
-    x = W.prefill_long(seed=3, device=DEV)
-    outs = {}
-    for m in METHODS:
-        outs[m] = _prefill(x, m)
-    (oc, sc), (orr, sr), (ot, st) = outs["chunked"], outs["recurrent"], outs["tcgen05"]
-    assert_parity(oc, orr, sc, sr)
-    assert_parity(ot, orr, st, sr)
-    n = 2048
-    sub = {k: (v[:n].cpu() if isinstance(v, torch.Tensor) and v.shape[0] == 16 * 8192 else v)
-           for k, v in x.items()}
-    sub["state"] = x["state"][:1].cpu()
-    sub["cu_seqlens"] = torch.tensor([0, n], dtype=torch.int32)
-    sub["A_log"], sub["dt_bias"] = x["A_log"].cpu(), x["dt_bias"].cpu()
-    ro, rs = _oracle(sub)
-    for m in ("chunked", "tcgen05"):
-        o2, s2 = _prefill(sub, m)
-        assert_parity(o2.cpu(), ro, s2.cpu(), rs)
+def test_long_prefill_full_size_against_oracle():
+    """The whole 16 x 8192 long-prefill workload (131072 tokens, Hq 16, Hv 32, nonzero
+    state, decay in [0.5, 0.999]) through auto (the tcgen05 pipeline) and the two other
+    CUDA kernels, every output element and the full new state against the C oracle."""
+    x = W.prefill_long(seed=3)
+    assert fk.prefill_method(16 * 8192, num_seqs=16) == "tcgen05"
+    ro, rs = _oracle(x)
+    for m in ("auto", "chunked", "recurrent"):
+        o, s = _prefill(x, m)
+        assert_parity(o.cpu(), ro, s.cpu(), rs)
+        del o, s
+
+
+@pytest.mark.parametrize("norm_range", [(0.3, 1.0), (0.5, 1.4)])
+def test_unnormalised_keys_auto_at_256_plus_tokens(norm_range):
+    """Keys (and queries) that are not unit-norm, with norms in `norm_range` (beta |k|^2
+    up to 1.96, so single tokens can flip the sign of the state along k), at >= 256
+    packed tokens through auto (the tcgen05 pipeline), against the oracle."""
+    x = W.prefill_inputs([700, 300, 257], seed=55, Hq=4, Hv=8, decay_range=(0.9, 0.999))
+    g = torch.Generator().manual_seed(56)
+    lo, hi = norm_range
+    for key in ("q", "k"):
+        scale = torch.rand(x[key].shape[:2], generator=g) * (hi - lo) + lo
+        x[key] = (x[key].float() * scale[..., None]).to(torch.bfloat16)
+    assert fk.prefill_method(x["q"].shape[0], num_seqs=3) == "tcgen05"
+    o, s = _prefill(x, "auto")
+    ro, rs = _oracle(x)
+    assert_parity(o.cpu(), ro, s.cpu(), rs)
+
+
+def test_reference_distribution_with_qk_l2norm_auto_at_256_plus_tokens():
+    """The reference test's randn inputs at 512 tokens with use_qk_l2norm=True (the
+    normalisation Gated DeltaNet layers apply before the recurrence) through auto,
+    against the oracle's same option."""
+    rng = np.random.Generator(np.random.PCG64(6))
+    lengths, Hq, Hv = [300, 212], 4, 8
+    T = sum(lengths)
+    bf = lambda a: torch.from_numpy(a.astype(np.float32)).to(torch.bfloat16)
+    sn = rng.standard_normal
+    x = {"q": bf(sn((T, Hq, 128))), "k": bf(sn((T, Hq, 128))), "v": bf(sn((T, Hv, 128))),
+         "state": torch.from_numpy(sn((2, Hv, 128, 128)).astype(np.float32)),
+         "A_log": torch.from_numpy(sn(Hv).astype(np.float32)), "a": bf(sn((T, Hv))),
+         "dt_bias": torch.from_numpy(sn(Hv).astype(np.float32)), "b": bf(sn((T, Hv))),
+         "cu_seqlens": torch.tensor([0, 300, T], dtype=torch.int32), "scale": 1.0 / np.sqrt(128)}
+    o, s = _prefill(x, "auto", use_qk_l2norm=True)
+    ro, rs = c_oracle.prefill(x["q"], x["k"], x["v"], x["state"], x["A_log"], x["a"], x["dt_bias"],
+                              x["b"], x["cu_seqlens"], x["scale"], qk_l2norm=True)
+    assert_parity(o.cpu(), ro, s.cpu(), rs)
 
 
 @pytest.mark.parametrize("method", METHODS)
@@ -296,6 +324,40 @@ def test_prefill_tc_wave_split_under_graph_capture():
     torch.cuda.synchronize()
     fk.device_status()
     assert torch.equal(og, o) and torch.equal(sg, s)
+    del graph
+
+
+def test_prefill_tc_eager_call_during_a_capture_that_holds_the_split():
+    """A capture that contains a split call (the library's second stream joins that
+    capture) and, before the capture ends, an eager 160-chain call on another stream:
+    the eager call must not touch the captured second stream (it runs unsplit on its own
+    stream), and both it and the graph's replay equal the plain eager result."""
+    x = W.prefill_inputs([300, 128, 257, 64, 200], seed=36)
+    g = _gpu(x)
+
+    def run(out=None, ns=None):
+        return fk.kernel(g["q"], g["k"], g["v"], g["state"], g["A_log"], g["a"], g["dt_bias"], g["b"],
+                         g["cu_seqlens"], g["scale"], method="tcgen05", output=out, new_state=ns)
+
+    o_ref, s_ref = run()
+    torch.cuda.synchronize()
+    o_eager = torch.empty_like(o_ref)
+    s_eager = torch.empty_like(s_ref)
+    other = torch.cuda.Stream()
+    cs = torch.cuda.Stream()
+    cs.wait_stream(torch.cuda.current_stream())
+    other.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=cs, capture_error_mode="relaxed"):
+        og, sg = run()
+        with torch.cuda.stream(other):
+            run(o_eager, s_eager)
+    other.synchronize()
+    graph.replay()
+    torch.cuda.synchronize()
+    fk.device_status()
+    assert torch.equal(o_eager, o_ref) and torch.equal(s_eager, s_ref)
+    assert torch.equal(og, o_ref) and torch.equal(sg, s_ref)
     del graph
 
 

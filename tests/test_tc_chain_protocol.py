@@ -26,6 +26,13 @@ W^T, [U | X] and O^T (per quadrant).
 
 The kernel's barrier counts are read from the source and compared with the model's.
 Planted protocol mistakes (a missing condition or wait) must be caught.
+
+The give-up path is modelled too: with `timeouts` on, any wait whose barrier is not
+complete may run out (the role raises the shared abort flag and stops), and once the
+flag is up every wait that is not yet satisfied returns false.  The issuing thread
+then waits for the last commit of every batch kind it issued and the copy thread for
+every copy it issued; the schedule must end with every role finished and no MMA or
+copy still in flight (the CTA frees TMEM and exits after the last role).
 """
 import os
 import random
@@ -72,6 +79,7 @@ class Bar:
 class Sim:
     def __init__(self, nch, plant=None):
         self.nch, self.plant = nch, plant
+        self.abort = False
         self.tags = {}
         self.copy_w = {}      # part -> in-flight copies writing it
         self.mma_r = {}       # part -> in-flight MMA batches reading it
@@ -79,7 +87,7 @@ class Sim:
         self.pipe = []        # in-order tensor pipe: ("mma", reads, writes) / ("commit", bar)
         self.copies = []      # in-flight copies: (part, tag, bar)
         counts = dict(tma0=1, tma1=1, wdone=1, udone=1, d=1, s=1, qs=4, w=4, ss=8, ds=8, tw=1, tu=1,
-                      free0=1, free1=1, oread=4)
+                      free0=1, free1=1, oread=4, stg=4)
         self.counts = counts
         self.b = {k: Bar(k, v) for k, v in counts.items()}
 
@@ -198,6 +206,11 @@ def mma10(sim, c):   # S += delta'^T K, O^T += delta^T P^T
 
 
 # ------------------------------------------------------------------ roles
+# A role yields ("wait", bar, k) for a bounded, abort-aware wait (it receives True, or
+# False once it gave up or saw the abort flag), ("drain", bar, k) for a wait on its own
+# asynchronous work (always satisfied in the end), ("sync", bar, k) for the prep warps'
+# staging hand-off (no timer of its own: false only once the flag is up), "spin" for a
+# probe round of the issuing thread, or None to let others run.
 def issuer(sim):
     b, nch, plant = sim.b, sim.nch, sim.plant
     n6w = n6u = n8 = n10 = 0
@@ -223,45 +236,79 @@ def issuer(sim):
             n6u += 1
             progress = True
         sim.progress = progress
+        if not progress and sim.abort:
+            break                                   # (the idle bookkeeping sees the flag)
+        if not progress and sim.timeouts and sim.rng.random() < 0.01:
+            sim.abort = True                        # the idle timer ran out
+            break
         yield "spin"
     for bar, n in (("wdone", n6w), ("udone", n6u), ("d", n8), ("s", n10)):
         if n:
-            yield ("wait", bar, n - 1)
+            yield ("drain", bar, n - 1)
     for c in range(max(0, n10 - 2), n10):
-        yield ("wait", f"free{c & 1}", c >> 1)
+        yield ("drain", f"free{c & 1}", c >> 1)
 
 
 def copier(sim):
+    issued = n_tw = n_tu = 0
+    failed = False
     for c in range(sim.nch):
         st = c & 1
-        if c >= 1:
-            yield ("wait", "wdone", c - 1)
+        if c >= 1 and not (yield ("wait", "wdone", c - 1)):
+            failed = True
+            break
         sim.copy([("T2",)], c, "tw", f"copy T''({c})")
-        if c >= 2 and sim.plant != "no_free_wait":
-            yield ("wait", f"free{st}", (c - 2) >> 1)
+        n_tw += 1
+        if c >= 2 and sim.plant != "no_free_wait" and not (yield ("wait", f"free{st}", (c - 2) >> 1)):
+            failed = True
+            break
         sim.copy(_stage(st), c, f"tma{st}", f"copy stage({c})")
-        if c >= 1:
-            yield ("wait", "udone", c - 1)
+        issued += 1
+        if c >= 1 and not (yield ("wait", "udone", c - 1)):
+            failed = True
+            break
         sim.copy([("T1",)], c, "tu", f"copy T'({c})")
+        n_tu += 1
         yield None
+    if sim.plant == "copy_drain_on_own_failure_only" and not failed:
+        return
+    for cc in range(max(0, issued - 2), issued):
+        yield ("drain", f"tma{cc & 1}", cc >> 1)
+    if n_tw:
+        yield ("drain", "tw", n_tw - 1)
+    if n_tu:
+        yield ("drain", "tu", n_tu - 1)
 
 
 def prep(sim, q):
     who = f"prep{q}"
     out_bar = "s"
+    nout = [0]
+    sync = "wait_forever" if sim.plant == "named_barrier" else "sync"
 
     def write_out(c):
         sim.read(("O", q), ("out", c), who)
         yield None
         sim.write(("O", q), ("zero", c + 1), who)
         sim.b["oread"].arrive()
-        yield None
+        j = nout[0]
+        nout[0] += 1
+        sim.b["stg"].arrive()
+        if not (yield (sync, "stg", 2 * j)):
+            return False
+        yield None                                  # bf16 rows into the staging tile
+        sim.b["stg"].arrive()
+        if not (yield (sync, "stg", 2 * j + 1)):
+            return False
+        yield None                                  # staging tile -> global rows
+        return True
 
     for c in range(sim.nch):
         st = c & 1
-        yield ("wait", f"tma{st}", c >> 1)
-        if c > 0:
-            yield ("wait", "d", c - 1)
+        if not (yield ("wait", f"tma{st}", c >> 1)):
+            break
+        if c > 0 and not (yield ("wait", "d", c - 1)):
+            break
         sim.read(("G", st), c, who)
         sim.read(("Q", st), c, who)
         yield None
@@ -270,7 +317,8 @@ def prep(sim, q):
             sim.write(("O", q), ("zero", 0), who)
         yield None
         sim.b["qs"].arrive()
-        yield ("wait", "wdone", c)
+        if not (yield ("wait", "wdone", c)):
+            break
         sim.read(("W", q), c, who)
         yield None
         sim.write(("WH", q), c, who)
@@ -278,10 +326,11 @@ def prep(sim, q):
         yield None
         sim.b["w"].arrive()
         if c > 0:
-            yield ("wait", out_bar, c - 1)
-            yield from write_out(c - 1)
-    if sim.nch:
-        yield ("wait", out_bar, sim.nch - 1)
+            if not (yield ("wait", out_bar, c - 1)):
+                break
+            if not (yield from write_out(c - 1)):
+                break
+    if not sim.abort and sim.nch and (yield ("wait", out_bar, sim.nch - 1)):
         yield from write_out(sim.nch - 1)
 
 
@@ -292,11 +341,13 @@ def state(sim, hs, q):
     s_bar, ss_bar = "s", "ss"
     sim.write(("S", hs, q), ("S", 0), who)
     yield None
+    ok = True
     for c in range(sim.nch):
         st = c & 1
-        if c > 0:
-            yield ("wait", s_bar, c - 1)
-        yield ("wait", f"tma{st}", c >> 1)
+        if c > 0 and not (ok := (yield ("wait", s_bar, c - 1))):
+            break
+        if not (ok := (yield ("wait", f"tma{st}", c >> 1))):
+            break
         sim.read(("G", st), c, who)
         sim.read(("S", hs, q), ("S", c), who)
         yield None
@@ -305,7 +356,8 @@ def state(sim, hs, q):
         sim.write(("S", hs, q), ("Sdec", c), who)
         yield None
         sim.b[ss_bar].arrive()
-        yield ("wait", "d", c)
+        if not (ok := (yield ("wait", "d", c))):
+            break
         sim.read(("UX", q), ("delta", c), who)
         sim.read(("G", st), c, who)
         yield None
@@ -313,61 +365,74 @@ def state(sim, hs, q):
             sim.write(("R", bl, q), ("dsplit", c), who)
         yield None
         sim.b["ds"].arrive()
-    if sim.nch:
-        yield ("wait", "s", sim.nch - 1)
+    if ok and sim.nch and (yield ("wait", "s", sim.nch - 1)):
         sim.read(("S", hs, q), ("S", sim.nch), who)
 
 
-def run(nch, seed, plant=None, max_steps=400000):
+def run(nch, seed, plant=None, max_steps=400000, timeouts=False):
     sim = Sim(nch, plant)
     rng = random.Random(seed)
+    sim.rng, sim.timeouts = rng, timeouts
     roles = {"issuer": issuer(sim), "copier": copier(sim)}
     roles.update({f"prep{q}": prep(sim, q) for q in Q4})
     roles.update({f"state{hs}.{q}": state(sim, hs, q) for hs in (0, 1) for q in Q4})
-    waiting = {}    # role -> (bar, k)
+    waiting = {}    # role -> (kind, bar, k)
     done = set()
 
-    def step(name):
+    def step(name, value=None):
         try:
-            r = next(roles[name])
+            r = roles[name].send(value)
         except StopIteration:
             done.add(name)
             return
-        if isinstance(r, tuple) and r[0] == "wait":
-            waiting[name] = (r[1], r[2])
+        if isinstance(r, tuple):
+            waiting[name] = r
 
+    for name in roles:      # start every coroutine (up to its first yield)
+        step(name)
     for _ in range(max_steps):
         live = [n for n in roles if n not in done]
-        if not live and not sim.pipe and not sim.copies:
+        if not live:
+            if sim.pipe or sim.copies:
+                raise ProtocolError(f"CTA exits with {len(sim.pipe)} MMA entries and {len(sim.copies)} "
+                                    "copies in flight")
             return sim
         ready = []
         for n in live:
             if n == "issuer" and n not in waiting:
                 continue
             if n in waiting:
-                bar, k = waiting[n]
-                if not sim.b[bar].test(k, n):
-                    continue
-            ready.append(("role", n))
+                kind, bar, k = waiting[n]
+                if sim.b[bar].test(k, n):
+                    ready.append(("role", n, True))
+                elif kind == "wait" and (sim.abort or (timeouts and rng.random() < 0.002)):
+                    ready.append(("role", n, False))
+                elif kind == "sync" and sim.abort:
+                    ready.append(("role", n, False))
+                continue
+            ready.append(("role", n, None))
         if sim.pipe:
-            ready.append(("pipe", None))
-        ready += [("copy", i) for i in range(len(sim.copies))]
+            ready.append(("pipe", None, None))
+        ready += [("copy", i, None) for i in range(len(sim.copies))]
         spinning = "issuer" in live and "issuer" not in waiting
         if not ready and not spinning:
             raise ProtocolError(f"deadlock: waiting {waiting}")
         if spinning and (not ready or rng.random() < 0.3):
             step("issuer")
-            if not ready and not sim.progress and "issuer" not in done and "issuer" not in waiting:
+            if (not ready and not sim.progress and "issuer" not in done and "issuer" not in waiting
+                    and not sim.timeouts):
                 raise ProtocolError(f"deadlock (issuer idle): waiting {waiting}")
             continue
-        kind, x = ready[rng.randrange(len(ready))]
+        kind, x, val = ready[rng.randrange(len(ready))]
         if kind == "pipe":
             sim.retire_pipe()
         elif kind == "copy":
             sim.retire_copy(x)
         else:
+            if val is False and not sim.abort:
+                sim.abort = True        # this wait ran out: raise the flag
             waiting.pop(x, None)
-            step(x)
+            step(x, val)
     raise ProtocolError("schedule did not finish")
 
 
@@ -388,6 +453,28 @@ def test_planted_protocol_mistakes_are_caught(plant):
     with pytest.raises(ProtocolError):
         for seed in range(200):
             run(5, seed, plant)
+
+
+@pytest.mark.parametrize("nch", [1, 2, 3, 5, 9])
+def test_give_up_path_terminates_with_nothing_in_flight(nch):
+    """Random waits run out: every role still finishes, nothing deadlocks, and no MMA
+    or copy is in flight when the CTA exits; some schedules give up early, some late."""
+    aborted = 0
+    for seed in range(150):
+        sim = run(nch, 7000 * nch + seed, timeouts=True)
+        aborted += sim.abort
+    assert aborted > 30
+
+
+@pytest.mark.parametrize("plant,nch,seeds", [("named_barrier", 4, 400),
+                                              ("copy_drain_on_own_failure_only", 1, 2000)])
+def test_planted_give_up_mistakes_are_caught(plant, nch, seeds):
+    """A staging hand-off that cannot give up (a named barrier) deadlocks once another
+    prep warp stopped; a copy thread that drains only after its own wait failed leaves
+    copies in flight when another role gave up."""
+    with pytest.raises(ProtocolError):
+        for seed in range(seeds):
+            run(nch, 31000 + seed, plant, timeouts=True)
 
 
 def test_barrier_counts_match_the_kernel():

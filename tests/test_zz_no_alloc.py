@@ -42,9 +42,10 @@ def test_noalloc_rejects_beyond_capacity():
 @pytest.mark.gpu
 def test_noalloc_matches_pooled_entry_point_twice():
     """Two calls in a row (different batches, the second reusing the array the first
-    filled) each equal the pooled-workspace entry point bit for bit."""
+    filled) each equal the pooled-workspace entry point bit for bit; the second call
+    takes no device memory (free memory does not drop across it)."""
     cases = [([1000, 37, 700, 64], 7), ([2048, 129, 1], 8)]
-    for lengths, seed in cases:
+    for i, (lengths, seed) in enumerate(cases):
         x = W.prefill_inputs(lengths, seed=seed, Hq=16, Hv=32)
         T, N = sum(lengths), len(lengths)
         assert ((T + 63) // 64 + N) * 32 * SLOT_BYTES <= CAPACITY
@@ -53,8 +54,12 @@ def test_noalloc_matches_pooled_entry_point_twice():
                                  g["dt_bias"], g["b"], g["cu_seqlens"], g["scale"], method="tcgen05")
         out = torch.full_like(o_ref, 3.0)
         ns = torch.full_like(s_ref, 3.0)
+        torch.cuda.synchronize()
+        free_before = torch.cuda.mem_get_info(DEV)[0]
         rc = _noalloc(g, out, ns)
         assert rc == 0, _lib.load().gdn_last_error()
         fk.device_status()
+        if i > 0:
+            assert torch.cuda.mem_get_info(DEV)[0] >= free_before, "the call took device memory"
         assert torch.equal(out, o_ref)
         assert torch.equal(ns, s_ref)
