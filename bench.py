@@ -10,9 +10,16 @@ in [0.5, 0.999]) through the reference-facing ``kernel`` entry point.
 the ``decode`` object reports the batched decode step (B=512, in-place state,
 fresh q/k/v/a/b per step) in seq/s and state GB/s against the HBM roofline.
 
-Multi-GPU (torchrun, one process per GPU): every rank runs its own copy of the
-workload (weak scaling; sequences and heads are independent, so there is no
-data-path collective).  Timing is device time (CUDA events), max over ranks.
+Multi-GPU (torchrun, one process per GPU), no data-path collective (sequences and
+heads are independent; the only collectives are the timing barrier and max):
+  * the headline step is weak-scaled: a global batch of 16 x N sequences of 8192
+    tokens, placed by sharding.plan_prefill (16 per rank);
+  * the ``mixed`` object is the strong-scaled mixed workload: 256 sequences with
+    log-uniform lengths in [128, 32768] (1.55 M tokens) placed by plan_prefill
+    (longest first on the least-loaded rank, load = tokens x v-heads), prefilled,
+    then 1024 decode steps on the states each rank keeps resident; it reports the
+    whole job's prefill tokens/s and decode sequence-steps/s and the load imbalance.
+Timing is device time (CUDA events), max over ranks.
 
 ``--impl reference`` times the reference's own CPU implementation of the path
 (the fp32 torch recurrence of solution/gdn_baseline_torch.py, restated in
@@ -81,11 +88,14 @@ def workload_name():
 
 def base_config(n_gpus):
     return {"workload": workload_name(), "n_seqs": N_SEQS, "seq_len": SEQ_LEN,
+            "global_batch_seqs": N_SEQS * n_gpus,
             "tokens_per_gpu_step": N_SEQS * SEQ_LEN, "num_qk_heads": 16, "num_v_heads": 32,
             "head_size": 128, "initial_state": "fp32 N(0,0.02^2)", "decay_range": [0.5, 0.999],
             "decode_workload": f"gdn_decode_b{DECODE_B}_inplace_{DECODE_STEPS}steps",
             "l2": "inputs larger than L2 (2.2 GB per prefill step, 1 GiB decode state)",
-            "parallelism": f"replicas{n_gpus} (sequence/head sharding, no collective)"}
+            "parallelism": (f"sharded{n_gpus}: a global batch of {N_SEQS * n_gpus} x {SEQ_LEN} sequences "
+                            f"placed by plan_prefill, {N_SEQS} per rank (weak scaling, no data-path "
+                            "collective)")}
 
 
 def cpu_prefill_sample(impl, budget_s):
@@ -163,6 +173,113 @@ def reference_arm(args):
     return 0
 
 
+MIXED_SEED, MIXED_SEQS, MIXED_STEPS = 4, 256, 1024
+
+
+def run_mixed(args, rank, world, dev, barrier, gather, peaks):
+    """The mixed prefill + decode workload, strong-scaled over the ranks (see the module
+    docstring); returns the ``mixed`` object (rank 0) or None."""
+    import fastaf_kernel_b200 as fk
+    from fastaf_kernel_b200 import sharding, workloads as W
+    lengths = W.mixed_lengths(MIXED_SEED, MIXED_SEQS)
+    plans = sharding.plan_prefill(lengths, world, 16, 32)
+    mine = plans[rank].items
+    spans = {(it.hq0, it.hq1) for it in mine}
+    # 256 sequences on at most 8 ranks: whole sequences, every rank all heads
+    assert len(spans) <= 1, "the mixed bench expects whole-sequence items"
+    hq0, hq1 = spans.pop() if spans else (0, 16)
+    seqs = [it.seq for it in mine]
+    x = W.mixed_shard(lengths, seqs, MIXED_SEED, device=dev, hq0=hq0, hq1=hq1)
+    n, T = len(seqs), int(x["cu_seqlens"][-1].item()) if seqs else 0
+    Hq_r, Hv_r = hq1 - hq0, 2 * (hq1 - hq0)
+    stream = torch.cuda.current_stream()
+    pre_ms = dec_ms = 0.0
+    if n:
+        out = torch.empty((T, Hv_r, 128), dtype=torch.bfloat16, device=dev)
+        ns = torch.empty((n, Hv_r, 128, 128), dtype=torch.float32, device=dev)
+
+        def prefill():
+            fk.kernel(x["q"], x["k"], x["v"], x["state"], x["A_log"], x["a"], x["dt_bias"], x["b"],
+                      x["cu_seqlens"], x["scale"], output=out, new_state=ns)
+    for _ in range(args.warmup):
+        if n:
+            prefill()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        if n:
+            prefill()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    pre_ms = e0.elapsed_time(e1) / args.steps
+    if n:
+        fk.device_status()
+    # 1024 decode steps on this rank's resident states (in place), fresh q/k/v/a/b per
+    # step, captured once as a CUDA graph (no host launch cost inside the timed replay)
+    graph = None
+    if n:
+        state = ns
+        steps_in = [W.decode_step_inputs(n, seed=50_000 + 7919 * rank + s, Hq=Hq_r, Hv=Hv_r, device=dev)
+                    for s in range(MIXED_STEPS)]
+        dout = torch.empty((n, 1, Hv_r, 128), dtype=torch.bfloat16, device=dev)
+
+        def decode(s):
+            st = steps_in[s]
+            fk.kernel_decode(st["q"], st["k"], st["v"], state, x["A_log"], st["a"], x["dt_bias"], st["b"],
+                             x["scale"], output=dout, new_state=state)
+        for s in range(args.warmup):
+            decode(s)
+        torch.cuda.synchronize()
+        cs = torch.cuda.Stream(dev)
+        cs.wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=cs):
+            for s in range(MIXED_STEPS):
+                decode(s)
+        graph.replay()          # warm
+        torch.cuda.synchronize()
+    barrier()
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d0.record(stream)
+    if graph is not None:
+        graph.replay()
+    d1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    dec_ms = d0.elapsed_time(d1)
+    del graph
+    rows = gather([float(n), float(T), float(plans[rank].load), pre_ms, dec_ms])
+    if rank != 0:
+        return None
+    pre = max(r[3] for r in rows)
+    dec = max(r[4] for r in rows)
+    total_tokens = sum(lengths)
+    mean = lambda v: sum(v) / len(v)
+    dec_bytes = MIXED_SEQS * W.bytes_per_decode_seq()
+    return {
+        "workload": f"gdn_mixed_{MIXED_SEQS}_loguniform_128_32768_then_{MIXED_STEPS}_decode_hq16_hv32_d128",
+        "scaling": "strong", "n_seqs": MIXED_SEQS, "prefill_tokens": total_tokens,
+        "parallelism": (f"sharded{world}: (sequence, v-head-group) items placed by plan_prefill "
+                        "(longest first, least-loaded rank, load = tokens x v-heads); states stay on "
+                        "their rank between prefill and decode; no data-path collective"),
+        "prefill_tokens_per_s": total_tokens / (pre / 1e3), "prefill_ms": pre,
+        "decode_seq_steps_per_s": MIXED_SEQS * MIXED_STEPS / (dec / 1e3), "decode_ms": dec,
+        "decode_gbs": dec_bytes * MIXED_STEPS / (dec / 1e3) / 1e9,
+        "decode_hbm_frac_per_gpu": dec_bytes * MIXED_STEPS / (dec / 1e3) / 1e9 / world / peaks["hbm_gbs"],
+        "job_ms": pre + dec,
+        "imbalance": {"planned_load_max_over_mean": max(r[2] for r in rows) / mean([r[2] for r in rows]),
+                      "prefill_ms_max_over_mean": pre / mean([r[3] for r in rows]),
+                      "decode_ms_max_over_mean": dec / mean([r[4] for r in rows])},
+        "per_rank": [{"rank": i, "seqs": int(r[0]), "tokens": int(r[1]), "prefill_ms": r[3], "decode_ms": r[4]}
+                     for i, r in enumerate(rows)],
+        "timing": f"prefill: mean of {args.steps} calls after {args.warmup} warm-up calls; decode: one replay "
+                  f"of a CUDA graph of {MIXED_STEPS} steps after a warm replay; max over ranks",
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -174,6 +291,7 @@ def main():
                     help="seconds of CPU work for the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-mixed", action="store_true", help="skip the mixed prefill + decode workload")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -201,6 +319,14 @@ def main():
         if world > 1:
             dist.barrier()
 
+    def gather(row):
+        """Per-rank rows of floats, on every rank (a sum of one-hot rows: no object pickling)."""
+        t = torch.zeros((world, len(row)), dtype=torch.float64, device=dev)
+        t[rank] = torch.tensor(row, dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t)
+        return t.cpu().tolist()
+
     def max_over_ranks(x: float) -> float:
         if world == 1:
             return x
@@ -209,6 +335,10 @@ def main():
         return float(t.item())
 
     # ---------------- prefill: inputs resident in HBM ----------------
+    # this rank's 16 sequences of the global batch (plan_prefill gives each rank 16)
+    from fastaf_kernel_b200 import sharding
+    plan = sharding.plan_prefill([SEQ_LEN] * (N_SEQS * world), world, 16, 32)
+    assert all(len(pl.items) == N_SEQS and all(it.hq1 - it.hq0 == 16 for it in pl.items) for pl in plan)
     x = W.prefill_long(seed=3 + rank, device=dev)
     T = N_SEQS * SEQ_LEN
     kernel_name = fk.prefill_method(T, args.method, N_SEQS)
@@ -226,7 +356,7 @@ def main():
     def prefill_step():
         fk.kernel(x["q"], x["k"], x["v"], x["state"], x["A_log"], x["a"], x["dt_bias"],
                   x["b"], x["cu_seqlens"], x["scale"], output=out, new_state=ns,
-                  method=args.method, validate=False)
+                  method=args.method)
 
     for _ in range(args.warmup):
         prefill_step()
@@ -332,7 +462,7 @@ def main():
                 d = S["x"]
                 fk.kernel(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"], d["dt_bias"], d["b"],
                           d["cu_seqlens"], d["scale"], output=S["out"], new_state=S["ns"],
-                          method=args.method, validate=False)
+                          method=args.method)
                 S["comp"].record(s_cmp)
             with torch.cuda.stream(s_d2h):
                 s_d2h.wait_event(S["comp"])
@@ -358,11 +488,21 @@ def main():
         e_ms = max_over_ranks(e0.elapsed_time(e1))
         e2e = {"value": world * T * n_e2e / (e_ms / 1e3), "unit": UNIT,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": n_e2e,
-               "path": "pinned host -> device copies, fastaf_kernel_b200.kernel, device -> "
+               "path": "pinned host -> device copies, fastaf_kernel_b200.kernel (default arguments), device -> "
                        "pinned host copies of output and new_state; two buffer sets on three "
                        "streams, so one step's copies overlap the neighbouring steps' compute"}
 
     clk.__exit__(None, None, None)
+
+    # ---------------- mixed prefill + decode workload, strong-scaled ----------------
+    mixed = None
+    if not args.no_mixed:
+        del x, out, ns, dsteps, d0, dstate, dout
+        if e2e is not None:
+            del sets, hx
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        mixed = run_mixed(args, rank, world, dev, barrier, gather, peaks)
 
     # ---------------- CPU baseline (rank 0, one GPU only) ----------------
     cpu = None
@@ -384,7 +524,7 @@ def main():
                                          "the benchmark configurations)",
                 "config": base_config(world), "roofline": roofline, "cpu_baseline": cpu,
                 "e2e": e2e, "gpu_launches": args.steps * launches_per_step, "clocks": clk.summary(),
-                "decode": decode, "launch_ms": launch_ms}
+                "decode": decode, "mixed": mixed, "launch_ms": launch_ms}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -144,20 +144,25 @@ __device__ __forceinline__ void issue_chunk(const CUtensorMap *qmap, const CUten
     tma_load_3d(vv + 8192, vmap, bar, 64, h, z);
 }
 
-// Bounded wait that gives up at once when another role has already given up.
+// Longest a waiting thread sleeps between looks at the abort flag and the clock.
+constexpr uint32_t kMaxSuspendNs = 1000000;
+
+// Bounded wait that gives up at once when another role has already given up.  Each
+// probe sleeps until the phase completes or min(limit, 1 ms) has passed, so the limit
+// holds to within one probe however short it is, and a thread whose barrier will never
+// complete (because another role gave up) notices the flag within 1 ms.
 __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, int site, volatile int *abort,
                                              uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
-    for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 63u) == 0) {
-            if (*abort) return false;
-            if (global_timer_ns() - t0 > limit_ns) {
-                atomicExch(&g_tc_error, site);
-                *abort = 1;
-                return false;
-            }
+    const uint32_t hint = limit_ns < kMaxSuspendNs ? static_cast<uint32_t>(limit_ns) : kMaxSuspendNs;
+    for (;;) {
+        if (mbar_try_wait_hint(bar, parity, hint)) return true;
+        if (*abort) return false;
+        if (global_timer_ns() - t0 > limit_ns) {
+            atomicExch(&g_tc_error, site);
+            *abort = 1;
+            return false;
         }
     }
 }
@@ -416,7 +421,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         auto stage_sync = [&](uint32_t parity) {
             warp_arrive(b_stg, lane);
             bool ok = true;
-            while (!mbar_try_wait(b_stg, parity)) {
+            while (!mbar_try_wait_hint(b_stg, parity, kMaxSuspendNs)) {
                 if (*abort) {
                     ok = false;
                     break;

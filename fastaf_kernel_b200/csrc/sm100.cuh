@@ -50,6 +50,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// try_wait with an explicit suspend-time limit: if the phase is not complete the thread
+// sleeps until it completes or about `hint_ns` have passed, whichever comes first (the
+// hint replaces the system-dependent limit of the plain form).
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
 // Non-blocking probe of the same condition (never suspends the thread): for loops
 // that poll several barriers.
 __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {

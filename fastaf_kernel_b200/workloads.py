@@ -7,7 +7,8 @@ and value distributions of the five benchmark configurations:
   prefill_varlen   4 sequences, lengths U[64, 512], half with a zero state
   decode_b512      B=512 decode, 100 steps, fresh q/k/v/a/b per step, in-place state
   prefill_long     16 x 8192 tokens, nonzero state, per-token decay in [0.5, 0.999]
-  mixed            256 sequences, log-uniform lengths in [128, 32768], then decode
+  mixed            256 sequences, log-uniform lengths in [128, 32768], then 1024 decode
+                   steps on the resident states (mixed_lengths, mixed_shard: any shard of it)
 
 Distributions: q, k ~ N(0,1) L2-normalised per head, then bf16; v ~ N(0,1) bf16;
 a, b ~ N(0,1) bf16; A_log = log U(1,16) fp32; dt_bias ~ U(-1,1) fp32;
@@ -130,6 +131,42 @@ def loguniform_lengths(seed: int, n: int = 256, lo: int = 128, hi: int = 32768) 
     g = _gen(seed, "cpu")
     u = torch.rand(n, generator=g, dtype=torch.float64)
     return [int(round(math.exp(math.log(lo) + float(x) * (math.log(hi) - math.log(lo))))) for x in u]
+
+
+def mixed_lengths(seed: int = 4, n: int = 256) -> List[int]:
+    """Sequence lengths of the mixed prefill + decode workload: 256 log-uniform in
+    [128, 32768] (1.55 M tokens at seed 4)."""
+    return loguniform_lengths(seed, n=n)
+
+
+def mixed_shard(lengths: List[int], seqs: List[int], seed: int, device="cpu", hq0: int = 0,
+                hq1: int = HQ, Hq: int = HQ, Hv: int = HV) -> Dict[str, torch.Tensor]:
+    """Packed prefill inputs of sequences `seqs` (in that order) of the mixed workload,
+    restricted to q/k heads [hq0, hq1) and their v-heads.  Sequence i is drawn from its
+    own seed (seed * 1_000_003 + i) and the head parameters from `seed`, so a sequence's
+    inputs are the same whichever rank holds it: every sharding of the batch computes
+    the same workload.  Every sequence has a nonzero N(0, 0.02^2) initial state."""
+    ratio = Hv // Hq
+    h0, h1 = hq0 * ratio, hq1 * ratio
+    A_log, dt_bias = head_params(seed + 1_000_003, Hv, device)
+    parts = {k: [] for k in ("q", "k", "v", "a", "b", "state")}
+    for i in seqs:
+        L = int(lengths[i])
+        g = _gen(seed * 1_000_003 + i, device)
+        parts["q"].append(_unit_bf16((L, Hq, D), g, device)[:, hq0:hq1])
+        parts["k"].append(_unit_bf16((L, Hq, D), g, device)[:, hq0:hq1])
+        parts["v"].append(_normal((L, Hv, D), g, device).to(torch.bfloat16)[:, h0:h1])
+        parts["a"].append(_normal((L, Hv), g, device).to(torch.bfloat16)[:, h0:h1])
+        parts["b"].append(_normal((L, Hv), g, device).to(torch.bfloat16)[:, h0:h1])
+        parts["state"].append(_normal((1, Hv, D, D), g, device, STATE_STD)[:, h0:h1])
+    n = len(seqs)
+    cu = torch.zeros(n + 1, dtype=torch.int32)
+    if n:
+        cu[1:] = torch.cumsum(torch.tensor([int(lengths[i]) for i in seqs], dtype=torch.int64), 0).to(torch.int32)
+    out = {k: (torch.cat(v).contiguous() if v else None) for k, v in parts.items()}
+    out.update({"A_log": A_log[h0:h1].contiguous(), "dt_bias": dt_bias[h0:h1].contiguous(),
+                "cu_seqlens": cu.to(device), "scale": 1.0 / math.sqrt(D)})
+    return out
 
 
 def prefill_varlen(seed: int = 1, device="cpu", Hq: int = HQ, Hv: int = HV):
