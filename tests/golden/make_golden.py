@@ -3,7 +3,7 @@
 Runs only where the reference checkout is present (it is not needed, and not
 read, by the tests):
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <path of the reference checkout>
 
 For each case in fixtures.CASES it regenerates the inputs, calls the
 reference's ``run`` (``solution/gdn_baseline_torch.py:12-91`` for Hq=16/Hv=32,
@@ -66,4 +66,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path of the reference checkout>")
+    main(sys.argv[1])

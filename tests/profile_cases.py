@@ -1,7 +1,8 @@
-"""Small, self-contained launches of each kernel for profiling under ncu.
+"""Small, self-contained launches of each kernel for profiling under ncu (the
+reproducer of the summaries under profiles/; not part of the library).
 
-    python -m fastaf_kernel_b200.profile_cases prefill --seq-len 4096 [--method tcgen05]
-    python -m fastaf_kernel_b200.profile_cases decode --batch 512
+    python tests/profile_cases.py prefill --seq-len 4096 [--method tcgen05]
+    python tests/profile_cases.py decode --batch 512
 
 Each case builds its seeded inputs on cuda:0, runs the kernel a few times (so a
 profiler can skip the first launch with `-s`) and exits 0.  Inputs are sized
@@ -12,12 +13,14 @@ one launch ends in seconds.
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 
 import torch
 
-from . import api
-from . import workloads as W
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+from fastaf_kernel_b200 import api  # noqa: E402
+from fastaf_kernel_b200 import workloads as W  # noqa: E402
 
 
 def prefill(seq_len: int, n_seqs: int, method: str, launches: int) -> None:
