@@ -176,6 +176,69 @@ def reference_arm(args):
 MIXED_SEED, MIXED_SEQS, MIXED_STEPS = 4, 256, 1024
 
 
+def reference_gpu_leg(args, x, out, ns, d0, dsteps, dout, our_prefill, our_dec_gbs, stream):
+    """The reference's own Triton GPU kernels (solution/triton/kernel.py:138-409, compiled
+    ahead of time for sm_100 into oracle/_ref/ by oracle/ref_triton.py) on the same inputs
+    as the timed prefill and decode steps, autotuned on this GPU as the reference's autotuner
+    would; a measured baseline beside cpu_baseline, not the product path."""
+    from oracle import ref_triton
+    if not ref_triton.available():
+        return {"unavailable": "oracle/_ref/ holds no compiled reference kernels (build() compiles them "
+                               "where the reference checkout is present)"}
+    from fastaf_kernel_b200 import workloads as W
+    ref = ref_triton.RefTriton()
+    T = x["q"].shape[0]
+
+    def prefill():
+        ref.prefill(x["q"], x["k"], x["v"], x["state"], x["A_log"], x["a"], x["dt_bias"], x["b"],
+                    x["cu_seqlens"], x["scale"], out, ns)
+    prefill()                        # autotunes: the fastest configuration of the list
+    for _ in range(args.warmup - 1):
+        prefill()
+    torch.cuda.synchronize()
+    steps = max(1, min(args.steps, 5))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        prefill()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    pre_ms = e0.elapsed_time(e1) / steps
+    B = d0["q"].shape[0]
+    new_state = torch.empty_like(d0["state"])
+    dec_out = dout.view(B, dout.shape[2], dout.shape[3])
+
+    def decode(s):
+        st = dsteps[s % len(dsteps)]
+        ref.decode(st["q"], st["k"], st["v"], d0["state"], d0["A_log"], st["a"], d0["dt_bias"], st["b"],
+                   d0["scale"], dec_out, new_state)
+    decode(0)
+    for s in range(1, args.warmup):
+        decode(s)
+    torch.cuda.synchronize()
+    dsteps_n = len(dsteps)
+    e0.record(stream)
+    for s in range(dsteps_n):
+        decode(s)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dec_ms = e0.elapsed_time(e1) / dsteps_n
+    dec_gbs = B * W.bytes_per_decode_seq() / (dec_ms / 1e3) / 1e9
+    del new_state
+    torch.cuda.empty_cache()
+    tps = T / (pre_ms / 1e3)
+    return {"kind": "the reference's Triton kernels (_gdn_prefill_kernel_v2, _gdn_decode_kernel_v3 of "
+                    "solution/triton/kernel.py), compiled for sm_100 from the reference sources, autotuned "
+                    "over their own configuration lists on this GPU",
+            "prefill": {"value": tps, "unit": UNIT, "ms_per_step": pre_ms, "steps": steps,
+                        "config": ref.config("prefill"), "configs_timed": ref.tried["prefill"],
+                        "ours_over_reference": our_prefill / tps},
+            "decode": {"value": dec_gbs, "unit": "GB/s", "ms_per_step": dec_ms, "steps": dsteps_n,
+                       "seq_per_s": B / (dec_ms / 1e3), "config": ref.config("decode"),
+                       "configs_timed": ref.tried["decode"], "ours_over_reference": our_dec_gbs / dec_gbs,
+                       "note": "out of place (the reference allocates a new state each step)"}}
+
+
 def run_mixed(args, rank, world, dev, barrier, gather, peaks):
     """The mixed prefill + decode workload, strong-scaled over the ranks (see the module
     docstring); returns the ``mixed`` object (rank 0) or None."""
@@ -292,6 +355,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-mixed", action="store_true", help="skip the mixed prefill + decode workload")
+    ap.add_argument("--no-ref-gpu", action="store_true",
+                    help="skip timing the reference's own Triton kernels on this GPU")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -428,6 +493,11 @@ def main():
                            "peak_source": peaks["source"],
                            "bytes_per_launch": dec_bytes}}
 
+    # ---------------- the reference's own Triton kernels on this GPU (rank 0, N = 1) ----------------
+    ref_gpu = None
+    if rank == 0 and world == 1 and not args.no_ref_gpu:
+        ref_gpu = reference_gpu_leg(args, x, out, ns, d0, dsteps, dout, value, dec_gbs, stream)
+
     # ---------------- end to end through the public API, host buffers ----------------
     e2e = None
     if not args.no_e2e:
@@ -524,7 +594,7 @@ def main():
                                          "the benchmark configurations)",
                 "config": base_config(world), "roofline": roofline, "cpu_baseline": cpu,
                 "e2e": e2e, "gpu_launches": args.steps * launches_per_step, "clocks": clk.summary(),
-                "decode": decode, "mixed": mixed, "launch_ms": launch_ms}
+                "decode": decode, "mixed": mixed, "reference_gpu": ref_gpu, "launch_ms": launch_ms}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
