@@ -174,6 +174,72 @@ def reference_arm(args):
 
 
 MIXED_SEED, MIXED_SEQS, MIXED_STEPS = 4, 256, 1024
+CP_TOKENS, CP_SEGMENTS_PER_RANK = 262144, 4
+
+
+def run_context_parallel(args, rank, world, dev, barrier, gather):
+    """One 262,144-token sequence (Hq 16, Hv 32, nonzero state, decay in [0.999, 0.99999])
+    prefilled by context_parallel.prefill_context_parallel over all ranks (each rank a
+    contiguous slice cut into 4 segments; one all-gather of the (M, C) state maps and one
+    broadcast of the final state over NCCL), beside the same sequence as one ordinary
+    prefill call on rank 0's GPU; returns the ``context_parallel`` object (rank 0)."""
+    import torch.distributed as dist
+    import fastaf_kernel_b200 as fk
+    from fastaf_kernel_b200 import context_parallel as cp, workloads as W
+    x = W.prefill_inputs([CP_TOKENS], seed=5, device=dev, decay_range=(0.999, 0.99999))
+    per = (CP_TOKENS // world) // 64 * 64
+    lo, hi = rank * per, (CP_TOKENS if rank == world - 1 else (rank + 1) * per)
+    sl = lambda t: t[lo:hi]
+    stream = torch.cuda.current_stream()
+
+    def parallel():
+        return cp.prefill_context_parallel(sl(x["q"]), sl(x["k"]), sl(x["v"]), x["state"], x["A_log"],
+                                           sl(x["a"]), x["dt_bias"], sl(x["b"]), x["scale"],
+                                           segments_per_rank=CP_SEGMENTS_PER_RANK)
+    for _ in range(args.warmup):
+        parallel()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = max(1, min(args.steps, 5))
+    e0.record(stream)
+    for _ in range(steps):
+        _, fin = parallel()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    cp_ms = e0.elapsed_time(e1) / steps
+    one_ms, rel = 0.0, 0.0
+    if rank == 0:
+        cu = torch.tensor([0, CP_TOKENS], dtype=torch.int32, device=dev)
+
+        def one_pass():
+            return fk.kernel(x["q"], x["k"], x["v"], x["state"], x["A_log"], x["a"], x["dt_bias"], x["b"],
+                             cu, x["scale"])
+        for _ in range(args.warmup):
+            _, s1 = one_pass()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(steps):
+            _, s1 = one_pass()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        one_ms = e0.elapsed_time(e1) / steps
+        rel = float(((fin - s1).abs().max() / s1.abs().max()).item())
+    rows = gather([cp_ms, one_ms, rel])
+    del x
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    par = max(r[0] for r in rows)
+    return {"workload": f"gdn_context_parallel_1x{CP_TOKENS}_hq16_hv32_d128", "scaling": "strong",
+            "segments_per_rank": CP_SEGMENTS_PER_RANK, "ranks": world, "ms": par,
+            "tokens_per_s": CP_TOKENS / (par / 1e3), "one_gpu_one_pass_ms": rows[0][1],
+            "speedup_vs_one_gpu_one_pass": rows[0][1] / par,
+            "final_state_max_rel_vs_one_pass": rows[0][2],
+            "exchange": "one NCCL all-gather of 3 x Hv x 128 x 128 float64 per rank, one broadcast of the "
+                        "final state",
+            "timing": f"mean of {steps} calls after {args.warmup} warm-up calls, max over ranks"}
 
 
 def reference_gpu_leg(args, x, out, ns, d0, dsteps, dout, our_prefill, our_dec_gbs, stream):
@@ -355,6 +421,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-mixed", action="store_true", help="skip the mixed prefill + decode workload")
+    ap.add_argument("--no-cp", action="store_true", help="skip the context-parallel prefill (N > 1)")
     ap.add_argument("--no-ref-gpu", action="store_true",
                     help="skip timing the reference's own Triton kernels on this GPU")
     args = ap.parse_args()
@@ -574,6 +641,13 @@ def main():
         torch.cuda.empty_cache()
         mixed = run_mixed(args, rank, world, dev, barrier, gather, peaks)
 
+    # ---------------- one long sequence over all ranks (N > 1) ----------------
+    cpar = None
+    if world > 1 and not args.no_cp:
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        cpar = run_context_parallel(args, rank, world, dev, barrier, gather)
+
     # ---------------- CPU baseline (rank 0, one GPU only) ----------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -594,7 +668,8 @@ def main():
                                          "the benchmark configurations)",
                 "config": base_config(world), "roofline": roofline, "cpu_baseline": cpu,
                 "e2e": e2e, "gpu_launches": args.steps * launches_per_step, "clocks": clk.summary(),
-                "decode": decode, "mixed": mixed, "reference_gpu": ref_gpu, "launch_ms": launch_ms}
+                "decode": decode, "mixed": mixed, "context_parallel": cpar, "reference_gpu": ref_gpu,
+                "launch_ms": launch_ms}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
