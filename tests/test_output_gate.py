@@ -53,32 +53,47 @@ def test_prefill_with_output_gate(method):
     _assert_close(o_gated, _reference(o_plain, z, w, 1e-5))
 
 
-def test_gated_prefill_is_bit_identical_to_two_calls():
-    """kernel(..., output_gate=) (gdn_prefill_gated) equals prefill, then output_gate."""
-    x = W.prefill_inputs([700, 129, 64, 1], seed=73, Hq=4, Hv=8, device=DEV)
+@pytest.mark.parametrize("lengths,Hq,Hv,wdtype", [
+    ([700, 129, 64, 1], 4, 8, torch.float32),          # partial chunks, a one-token sequence
+    ([300, 128, 257, 64, 200], 16, 32, torch.bfloat16),  # 160 chains: the wave split
+    ([256, 0, 191, 64, 300], 16, 32, torch.float32),     # an empty sequence among them
+])
+def test_gated_prefill_is_bit_identical_to_two_calls(lengths, Hq, Hv, wdtype):
+    """kernel(..., output_gate=) (gdn_prefill_gated; on tcgen05 the gating is applied in the
+    chains' output store) equals prefill, then output_gate, bit for bit; the state too."""
+    x = W.prefill_inputs(lengths, seed=73, Hq=Hq, Hv=Hv, device=DEV)
     T = x["q"].shape[0]
     g = torch.Generator(device=DEV).manual_seed(8)
-    z = torch.randn((T, 8, 128), generator=g, device=DEV).to(torch.bfloat16)
-    w = torch.rand(128, generator=g, device=DEV) + 0.5
+    z = torch.randn((T, Hv, 128), generator=g, device=DEV).to(torch.bfloat16)
+    w = (torch.rand(128, generator=g, device=DEV) + 0.5).to(wdtype)
     args = (x["q"], x["k"], x["v"], x["state"], x["A_log"], x["a"], x["dt_bias"], x["b"], x["cu_seqlens"], x["scale"])
-    o_fused, _ = fk.kernel(*args, method="tcgen05", output_gate=z, norm_weight=w)
-    o_plain, _ = fk.kernel(*args, method="tcgen05")
-    fk.output_gate(o_plain, z, w)
+    o_fused, s_fused = fk.kernel(*args, method="tcgen05", output_gate=z, norm_weight=w, norm_eps=1e-5)
+    o_plain, s_plain = fk.kernel(*args, method="tcgen05")
+    fk.output_gate(o_plain, z, w, 1e-5)
     fk.device_status()
     assert torch.equal(o_fused, o_plain)
+    assert torch.equal(s_fused, s_plain)
 
 
-def test_decode_with_output_gate():
-    d = W.decode_inputs(16, seed=72, Hq=4, Hv=8, device=DEV)
+@pytest.mark.parametrize("B,Hq,Hv,l2norm", [(16, 4, 8, False), (3, 16, 32, True), (512, 16, 32, False)])
+def test_decode_with_output_gate(B, Hq, Hv, l2norm):
+    """kernel_decode(..., output_gate=) (gdn_decode_gated: the gating in the decode kernel's
+    store) equals decode, then output_gate, bit for bit; in place, the state too."""
+    d = W.decode_inputs(B, seed=72, Hq=Hq, Hv=Hv, device=DEV)
     g = torch.Generator(device=DEV).manual_seed(7)
-    z = torch.randn((16, 1, 8, 128), generator=g, device=DEV).to(torch.bfloat16)
+    z = torch.randn((B, 1, Hv, 128), generator=g, device=DEV).to(torch.bfloat16)
     w = (torch.rand(128, generator=g, device=DEV) + 0.5).to(torch.bfloat16)
-    args = (d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"], d["dt_bias"], d["b"], d["scale"])
-    o_plain, s_plain = fk.kernel_decode(*args)
-    o_gated, s_gated = fk.kernel_decode(*args, output_gate=z, norm_weight=w)
+    st_plain, st_gated = d["state"].clone(), d["state"].clone()
+    args = lambda st: (d["q"], d["k"], d["v"], st, d["A_log"], d["a"], d["dt_bias"], d["b"], d["scale"])
+    o_plain, _ = fk.kernel_decode(*args(st_plain), new_state=st_plain, use_qk_l2norm=l2norm)
+    o_gated, _ = fk.kernel_decode(*args(st_gated), new_state=st_gated, use_qk_l2norm=l2norm,
+                                  output_gate=z, norm_weight=w, norm_eps=1e-5)
+    o_two = o_plain.clone()
+    fk.output_gate(o_two, z, w, 1e-5)
     fk.device_status()
-    assert torch.equal(s_gated, s_plain)
-    _assert_close(o_gated, _reference(o_plain, z, w, 1e-6))
+    assert torch.equal(st_gated, st_plain)
+    assert torch.equal(o_gated, o_two)
+    _assert_close(o_gated, _reference(o_plain, z, w, 1e-5))
 
 
 def test_output_gate_rejects_bad_arguments():
