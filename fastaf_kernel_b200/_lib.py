@@ -32,7 +32,7 @@ GDN_FLAG_QK_L2NORM = 1
 # Every symbol include/gdn_b200.h declares.
 EXPORTED_SYMBOLS = ("gdn_prefill", "gdn_prefill_ex", "gdn_prefill_ws", "gdn_prefill_workspace_size",
                     "gdn_prefill_resolve", "gdn_prefill_tc_launches", "gdn_prefill_noalloc", "gdn_prefill_flags",
-                    "gdn_prefill_gated",
+                    "gdn_prefill_gated", "gdn_prefill_strided", "gdn_decode_strided",
                     "gdn_decode", "gdn_decode_flags", "gdn_output_gate", "gdn_device_status",
                     "gdn_set_wait_limit_ns", "gdn_last_error", "gdn_version")
 
@@ -89,6 +89,11 @@ def load() -> ctypes.CDLL:
         lib.gdn_decode_flags.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i64, i32, i32, i32, f32,
                                          i32, i32, vp, vp, i32, vp]
         lib.gdn_decode_flags.restype = i32
+        lib.gdn_prefill_strided.argtypes = prefill_args + [i64, i64, i32, i32, vp]
+        lib.gdn_prefill_strided.restype = i32
+        lib.gdn_decode_strided.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i64, i32, i32, i32, f32,
+                                           i32, i32, vp, vp, i64, i64, i32, vp]
+        lib.gdn_decode_strided.restype = i32
         lib.gdn_prefill_flags.argtypes = prefill_args + [i32, i32, vp]
         lib.gdn_prefill_flags.restype = i32
         lib.gdn_prefill_gated.argtypes = prefill_args + [vp, vp, i32, f32, i32, i32, vp]

@@ -88,6 +88,23 @@ def _gate(t: torch.Tensor) -> torch.Tensor:
     return t.contiguous()
 
 
+def _gate_rows(t: torch.Tensor, Hv: int) -> Tuple[torch.Tensor, int]:
+    """Gate inputs a or b as the kernels read them: rows of Hv elements, element h of row r
+    at r * stride + h.  A view whose last dimension is contiguous, in fp32 or bf16 -- such
+    as a slice of the projection GEMM's output that holds a and b side by side -- passes as
+    it is, with its row stride in elements (0 when packed); anything else becomes a packed
+    copy (fp32 unless bf16)."""
+    if t.dtype not in _GATE_DTYPES:
+        t = t.float()
+    lead = [st for n, st in zip(t.shape[:-1], t.stride()[:-1]) if n != 1]
+    if t.dim() >= 1 and t.shape[-1] == Hv and (t.stride(-1) == 1 or Hv == 1):
+        if not lead:
+            return t, 0
+        if len(lead) == 1 and lead[0] >= Hv:
+            return t, (0 if lead[0] == Hv else int(lead[0]))
+    return t.contiguous(), 0
+
+
 def _scale(scale, D: int) -> float:
     # solution/triton/kernel.py:438-439: a falsy scale selects 1/sqrt(D).
     if not scale or scale == 0.0:
@@ -153,9 +170,13 @@ def kernel(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: Optional[to
     scale = _scale(scale, D)
 
     q, k, v = _bf16("q", q), _bf16("k", k), _bf16("v", v)
-    a, b, A_log, dt_bias = _gate(a), _gate(b), _gate(A_log), _gate(dt_bias)
+    # a and b may be views into a wider projection output (read through their row stride)
+    (a, sa), (b, sb) = _gate_rows(a, Hv), _gate_rows(b, Hv)
+    A_log, dt_bias = _gate(A_log), _gate(dt_bias)
     if a.dtype != b.dtype:
-        b = b.to(a.dtype)
+        b, sb = b.to(a.dtype).contiguous(), 0
+    if (sa or sb) and (output_gate is not None or norm_weight is not None):
+        (a, sa), (b, sb) = (a.contiguous(), 0), (b.contiguous(), 0)   # the gated entry takes packed gates
     if A_log.dtype != dt_bias.dtype:
         dt_bias = dt_bias.to(A_log.dtype)
     if state is not None:
@@ -180,7 +201,13 @@ def kernel(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: Optional[to
     ctx, stream = _on_device(device)
     with ctx:
         flags = _lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm else 0
-        if output_gate is None and norm_weight is None:
+        if output_gate is None and norm_weight is None and (sa or sb):
+            _lib.check(lib.gdn_prefill_strided(
+                _ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias),
+                _ptr(b), _ptr(cu), N, T, Hq, Hv, D, scale, _GATE_DTYPES[a.dtype],
+                _GATE_DTYPES[A_log.dtype], _ptr(output), _ptr(new_state), sa, sb, _METHODS[method], flags,
+                stream))
+        elif output_gate is None and norm_weight is None:
             _lib.check(lib.gdn_prefill_flags(
                 _ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias),
                 _ptr(b), _ptr(cu), N, T, Hq, Hv, D, scale, _GATE_DTYPES[a.dtype],
@@ -216,9 +243,11 @@ def _prepare_decode(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_sta
         raise ValueError(f"A_log and dt_bias must have Hv={Hv} elements")
     scale = _scale(scale, D)
     q, k, v = _bf16("q", q), _bf16("k", k), _bf16("v", v)
-    a, b, A_log, dt_bias = _gate(a), _gate(b), _gate(A_log), _gate(dt_bias)
+    # a and b may be views into a wider projection output (read through their row stride)
+    (a, sa), (b, sb) = _gate_rows(a, Hv), _gate_rows(b, Hv)
+    A_log, dt_bias = _gate(A_log), _gate(dt_bias)
     if a.dtype != b.dtype:
-        b = b.to(a.dtype)
+        b, sb = b.to(a.dtype).contiguous(), 0
     if A_log.dtype != dt_bias.dtype:
         dt_bias = dt_bias.to(A_log.dtype)
     inplace = new_state is not None and state is not None and new_state.data_ptr() == state.data_ptr()
@@ -242,7 +271,7 @@ def _prepare_decode(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_sta
           or not new_state.is_contiguous() or new_state.device != device):
         raise ValueError("new_state must be a contiguous fp32 [B, Hv, D, D] tensor on q's device")
 
-    return q, k, v, state, A_log, a, dt_bias, b, output, new_state, B, Hq, Hv, D, scale
+    return q, k, v, state, A_log, a, dt_bias, b, output, new_state, B, Hq, Hv, D, scale, sa, sb
 
 
 def kernel_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
@@ -260,16 +289,16 @@ def kernel_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     new_state [B, Hv, D, D] fp32).  Pass ``new_state=state`` to update the state
     in place (no second 2 MiB-per-sequence buffer).
     """
-    (q, k, v, state, A_log, a, dt_bias, b, output, new_state, B, Hq, Hv, D, scale) = _prepare_decode(
+    (q, k, v, state, A_log, a, dt_bias, b, output, new_state, B, Hq, Hv, D, scale, sa, sb) = _prepare_decode(
         q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state)
     device = q.device
     lib = _lib.load()
     ctx, stream = _on_device(device)
     with ctx:
-        _lib.check(lib.gdn_decode_flags(
+        _lib.check(lib.gdn_decode_strided(
             _ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias),
             _ptr(b), B, Hq, Hv, D, scale, _GATE_DTYPES[a.dtype], _GATE_DTYPES[A_log.dtype],
-            _ptr(output), _ptr(new_state), _lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm else 0,
+            _ptr(output), _ptr(new_state), sa, sb, _lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm else 0,
             stream))
     if output_gate is not None or norm_weight is not None:
         _gated_rmsnorm(output, output_gate, norm_weight, norm_eps)
@@ -337,12 +366,12 @@ def decode_step(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: torch.
         if u.data_ptr() != t.data_ptr():
             raise ValueError(f"decode_step needs {name} contiguous in a dtype the kernel reads directly "
                              "(with a and b of one dtype, A_log and dt_bias of one dtype)")
-    q, k, v, state, A_log, a, dt_bias, b, output, new_state, B, Hq, Hv, D, scale = prep
+    q, k, v, state, A_log, a, dt_bias, b, output, new_state, B, Hq, Hv, D, scale, sa, sb = prep
     device = q.device
     lib = _lib.load()
-    fn = lib.gdn_decode_flags
+    fn = lib.gdn_decode_strided
     head = (_ptr(q), _ptr(k), _ptr(v), _ptr(state), _ptr(A_log), _ptr(a), _ptr(dt_bias), _ptr(b), B, Hq, Hv, D,
-            scale, _GATE_DTYPES[a.dtype], _GATE_DTYPES[A_log.dtype], _ptr(output), _ptr(new_state),
+            scale, _GATE_DTYPES[a.dtype], _GATE_DTYPES[A_log.dtype], _ptr(output), _ptr(new_state), sa, sb,
             _lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm else 0)
     index = device.index
     # the raw handle of a device's current stream without building a Stream object

@@ -137,7 +137,21 @@ int gdn_decode_flags(const void *q, const void *k, const void *v, const float *s
                      int64_t batch, int num_qk_heads, int num_v_heads, int head_size, float scale,
                      int gate_dtype, int param_dtype, void *output, float *new_state, int flags,
                      void *stream) {
+    return gdn_decode_strided(q, k, v, state, A_log, a, dt_bias, b, batch, num_qk_heads, num_v_heads, head_size,
+                              scale, gate_dtype, param_dtype, output, new_state, 0, 0, flags, stream);
+}
+
+int gdn_decode_strided(const void *q, const void *k, const void *v, const float *state,
+                       const void *A_log, const void *a, const void *dt_bias, const void *b,
+                       int64_t batch, int num_qk_heads, int num_v_heads, int head_size, float scale,
+                       int gate_dtype, int param_dtype, void *output, float *new_state,
+                       int64_t a_row_stride, int64_t b_row_stride, int flags, void *stream) {
     g_last_error[0] = '\0';
+    if ((a_row_stride != 0 && a_row_stride < num_v_heads) || (b_row_stride != 0 && b_row_stride < num_v_heads) ||
+        a_row_stride > 0x7fffffff || b_row_stride > 0x7fffffff)
+        return fail(GDN_ERR_INVALID_ARGUMENT,
+                    "a/b row strides (%lld, %lld) must be 0 or in [num_v_heads=%d, 2^31)",
+                    (long long)a_row_stride, (long long)b_row_stride, num_v_heads);
     if (flags & ~GDN_FLAG_QK_L2NORM) return fail(GDN_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
     int rc = check_common(num_qk_heads, num_v_heads, head_size, gate_dtype, param_dtype, q, k, v,
                           A_log, a, dt_bias, b, output, new_state);
@@ -154,6 +168,8 @@ int gdn_decode_flags(const void *q, const void *k, const void *v, const float *s
     gdn::DecodeArgs p{q, k, v, state, A_log, a, dt_bias, b, batch, num_qk_heads, num_v_heads,
                       scale == 0.0f ? 1.0f / sqrtf(static_cast<float>(head_size)) : scale,
                       gate_dtype, param_dtype, output, new_state, (flags & GDN_FLAG_QK_L2NORM) ? 1 : 0};
+    p.a_stride = a_row_stride;
+    p.b_stride = b_row_stride;
     return cuda_status(gdn::launch_decode(p, static_cast<cudaStream_t>(stream)), "gdn_decode launch");
 }
 
@@ -167,6 +183,30 @@ static int gate_output(const gdn::PrefillArgs &p, cudaStream_t s) {
                        "gdn_prefill output gate launch");
 }
 
+// The tcgen05 prefill of a validated call: workspace from the caller or the pool.
+static int prefill_tc_call(const gdn::PrefillArgs &p, void *workspace, size_t workspace_bytes, cudaStream_t s) {
+    if (!gdn::prefill_tc_supported(p))
+        return fail(GDN_ERR_UNSUPPORTED,
+                    "the tcgen05 prefill needs an sm_100 device and total_tokens >= 64");
+    const size_t need = gdn::prefill_tc_workspace_bytes(p);
+    if (workspace) {
+        if (workspace_bytes < need)
+            return fail(GDN_ERR_INVALID_ARGUMENT, "workspace of %zu bytes is smaller than the %zu needed",
+                        workspace_bytes, need);
+        const cudaError_t e = gdn::launch_prefill_tc(p, workspace, s);
+        if (e != cudaSuccess) return cuda_status(e, "gdn_prefill (tcgen05) launch");
+        return gate_output(p, s);
+    }
+    void *ws = nullptr;
+    cudaError_t e = pool_alloc(&ws, need, s);
+    if (e != cudaSuccess) return cuda_status(e, "gdn_prefill (tcgen05) workspace");
+    e = gdn::launch_prefill_tc(p, ws, s, /*overlap=*/true);
+    const cudaError_t ef = cudaFreeAsync(ws, s);
+    if (e != cudaSuccess) return cuda_status(e, "gdn_prefill (tcgen05) launch");
+    if (ef != cudaSuccess) return cuda_status(ef, "gdn_prefill (tcgen05) workspace release");
+    return gate_output(p, s);
+}
+
 static int prefill_impl(const void *q, const void *k, const void *v, const float *state,
                         const void *A_log, const void *a, const void *dt_bias, const void *b,
                         const int32_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
@@ -174,9 +214,15 @@ static int prefill_impl(const void *q, const void *k, const void *v, const float
                         int gate_dtype, int param_dtype, void *output, float *new_state,
                         int method, void *workspace, size_t workspace_bytes, void *stream,
                         int flags = 0, const void *out_gate = nullptr, const void *norm_w = nullptr,
-                        int norm_w_dtype = 0, float norm_eps = 0.0f) {
+                        int norm_w_dtype = 0, float norm_eps = 0.0f, int64_t a_stride = 0,
+                        int64_t b_stride = 0) {
     g_last_error[0] = '\0';
     if (flags & ~GDN_FLAG_QK_L2NORM) return fail(GDN_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
+    if ((a_stride != 0 && a_stride < num_v_heads) || (b_stride != 0 && b_stride < num_v_heads) ||
+        a_stride > 0x7fffffff || b_stride > 0x7fffffff)
+        return fail(GDN_ERR_INVALID_ARGUMENT,
+                    "a/b row strides (%lld, %lld) must be 0 or in [num_v_heads=%d, 2^31)",
+                    (long long)a_stride, (long long)b_stride, num_v_heads);
     int rc = check_common(num_qk_heads, num_v_heads, head_size, gate_dtype, param_dtype, q, k, v,
                           A_log, a, dt_bias, b, output, new_state);
     if (rc) return rc;
@@ -206,6 +252,8 @@ static int prefill_impl(const void *q, const void *k, const void *v, const float
     p.norm_w_dtype = norm_w_dtype;
     p.norm_eps = norm_eps;
     p.status = gdn::device_status_word();
+    p.a_stride = a_stride;
+    p.b_stride = b_stride;
     const auto s = static_cast<cudaStream_t>(stream);
     if (flags & GDN_FLAG_QK_L2NORM) {
         // Normalised q and k into pool scratch, then the prefill on them.
@@ -214,7 +262,7 @@ static int prefill_impl(const void *q, const void *k, const void *v, const float
             return prefill_impl(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs, total_tokens,
                                 num_qk_heads, num_v_heads, head_size, scale, gate_dtype, param_dtype, output,
                                 new_state, method, workspace, workspace_bytes, stream, 0, out_gate, norm_w,
-                                norm_w_dtype, norm_eps);
+                                norm_w_dtype, norm_eps, a_stride, b_stride);
         void *qk = nullptr;
         cudaError_t e = pool_alloc(&qk, 2 * qk_bytes, s);
         if (e != cudaSuccess) return cuda_status(e, "gdn_prefill (qk l2norm) scratch");
@@ -225,35 +273,14 @@ static int prefill_impl(const void *q, const void *k, const void *v, const float
                                                   total_tokens, num_qk_heads, num_v_heads, head_size, scale,
                                                   gate_dtype, param_dtype, output, new_state, method, workspace,
                                                   workspace_bytes, stream, 0, out_gate, norm_w, norm_w_dtype,
-                                                  norm_eps);
+                                                  norm_eps, a_stride, b_stride);
         const cudaError_t ef = cudaFreeAsync(qk, s);
         if (rc2 != GDN_OK) return rc2;
         return cuda_status(ef, "gdn_prefill (qk l2norm) scratch release");
     }
     // auto: gdn_prefill_resolve's choice
     if (method == GDN_PREFILL_AUTO) method = gdn_prefill_resolve(total_tokens, num_seqs, method);
-    if (method == GDN_PREFILL_TCGEN05) {
-        if (!gdn::prefill_tc_supported(p))
-            return fail(GDN_ERR_UNSUPPORTED,
-                        "the tcgen05 prefill needs an sm_100 device and total_tokens >= 64");
-        const size_t need = gdn::prefill_tc_workspace_bytes(p);
-        if (workspace) {
-            if (workspace_bytes < need)
-                return fail(GDN_ERR_INVALID_ARGUMENT, "workspace of %zu bytes is smaller than the %zu needed",
-                            workspace_bytes, need);
-            const cudaError_t e = gdn::launch_prefill_tc(p, workspace, s);
-            if (e != cudaSuccess) return cuda_status(e, "gdn_prefill (tcgen05) launch");
-            return gate_output(p, s);
-        }
-        void *ws = nullptr;
-        cudaError_t e = pool_alloc(&ws, need, s);
-        if (e != cudaSuccess) return cuda_status(e, "gdn_prefill (tcgen05) workspace");
-        e = gdn::launch_prefill_tc(p, ws, s, /*overlap=*/true);
-        const cudaError_t ef = cudaFreeAsync(ws, s);
-        if (e != cudaSuccess) return cuda_status(e, "gdn_prefill (tcgen05) launch");
-        if (ef != cudaSuccess) return cuda_status(ef, "gdn_prefill (tcgen05) workspace release");
-        return gate_output(p, s);
-    }
+    if (method == GDN_PREFILL_TCGEN05) return prefill_tc_call(p, workspace, workspace_bytes, s);
     const bool chunked_ok = gdn::prefill_chunked_supported(p);
     if (method == GDN_PREFILL_CHUNKED && !chunked_ok)
         return fail(GDN_ERR_UNSUPPORTED, "the chunked tensor-core prefill is not available here");
@@ -283,6 +310,18 @@ int gdn_prefill_flags(const void *q, const void *k, const void *v, const float *
     return prefill_impl(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs, total_tokens,
                         num_qk_heads, num_v_heads, head_size, scale, gate_dtype, param_dtype, output,
                         new_state, method, nullptr, 0, stream, flags);
+}
+
+int gdn_prefill_strided(const void *q, const void *k, const void *v, const float *state,
+                        const void *A_log, const void *a, const void *dt_bias, const void *b,
+                        const int32_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
+                        int num_qk_heads, int num_v_heads, int head_size, float scale,
+                        int gate_dtype, int param_dtype, void *output, float *new_state,
+                        int64_t a_row_stride, int64_t b_row_stride, int method, int flags, void *stream) {
+    return prefill_impl(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs, total_tokens,
+                        num_qk_heads, num_v_heads, head_size, scale, gate_dtype, param_dtype, output,
+                        new_state, method, nullptr, 0, stream, flags, nullptr, nullptr, 0, 0.0f, a_row_stride,
+                        b_row_stride);
 }
 
 int gdn_prefill_gated(const void *q, const void *k, const void *v, const float *state,

@@ -69,6 +69,7 @@ struct PrepParams {
     float *ws_g;
     __nv_bfloat16 *ws_P;
     int64_t group0;   // (sequence, v-head group) index of blockIdx.x = 0
+    int sa, sb;       // elements between consecutive tokens' gate inputs in a, b
 };
 
 // [64][128] bf16 rows t0.. of head hh into 256-byte swizzled rows; rows past T read
@@ -144,7 +145,9 @@ __device__ __forceinline__ void store_block(const float (&acc)[NT][4], float sgn
         }
 }
 
-template <int NH>
+// kStrided: a and b are read through their row strides (views into a wider projection
+// output); the packed instantiation reads them at t * Hv + h, as before.
+template <int NH, bool kStrided>
 __global__ void __launch_bounds__(kThreads, 4) chunk_prep_kernel(const PrepParams p) {
     extern __shared__ __align__(1024) uint8_t sm[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -180,8 +183,8 @@ __global__ void __launch_bounds__(kThreads, 4) chunk_prep_kernel(const PrepParam
         for (int u = 0; u < 2; ++u) {
             const int64_t t = tb + lane + 32 * u;
             if (t < s1) {
-                ga[u] = load_scalar(p.a, t * p.Hv + hw, p.gate_dtype);
-                gb[u] = load_scalar(p.b, t * p.Hv + hw, p.gate_dtype);
+                ga[u] = load_scalar(p.a, t * (kStrided ? p.sa : p.Hv) + hw, p.gate_dtype);
+                gb[u] = load_scalar(p.b, t * (kStrided ? p.sb : p.Hv) + hw, p.gate_dtype);
             }
         }
     };
@@ -442,13 +445,16 @@ cudaError_t launch_chunk_prep(const PrefillArgs &p, uint8_t *ws_T, __nv_bfloat16
     if (chains == 0) return cudaSuccess;
     if (chains > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
     const int groups = prep_groups(chains);
-    auto kernel = nh == 2 ? chunk_prep_kernel<2> : chunk_prep_kernel<1>;
+    const bool strided = (p.a_stride && p.a_stride != p.Hv) || (p.b_stride && p.b_stride != p.Hv);
+    auto kernel = strided ? (nh == 2 ? chunk_prep_kernel<2, true> : chunk_prep_kernel<1, true>)
+                          : (nh == 2 ? chunk_prep_kernel<2, false> : chunk_prep_kernel<1, false>);
     const uint32_t smem = smem_bytes(nh);
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     PrepParams pp{static_cast<const __nv_bfloat16 *>(p.q), static_cast<const __nv_bfloat16 *>(p.k), p.A_log,
                   p.a, p.dt_bias, p.b, p.cu_seqlens, p.total_tokens, p.Hq, p.Hv, groups, p.gate_dtype,
-                  p.param_dtype, ws_T, ws_g, ws_P, chain_begin / nh};
+                  p.param_dtype, ws_T, ws_g, ws_P, chain_begin / nh,
+                  static_cast<int>(p.a_stride ? p.a_stride : p.Hv), static_cast<int>(p.b_stride ? p.b_stride : p.Hv)};
     kernel<<<dim3(static_cast<unsigned>(chains), groups), kThreads, smem, stream>>>(pp);
     return cudaGetLastError();
 }

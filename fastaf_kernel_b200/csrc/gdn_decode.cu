@@ -50,7 +50,7 @@ decode_kernel(const __nv_bfloat16 *__restrict__ q, const __nv_bfloat16 *__restri
               const __nv_bfloat16 *__restrict__ v, const float *state, const void *A_log,
               const void *a, const void *dt_bias, const void *b, int Hq, int Hv, float scale,
               int gate_dtype, int param_dtype, __nv_bfloat16 *__restrict__ out,
-              float *new_state) {
+              float *new_state, int sa, int sb) {
     constexpr int kRowsPerCta = kRowsPerPass * ROWS_PER_THREAD;
     constexpr int kCtasPerHead = kHeadDim / kRowsPerCta;
     const int64_t bh = blockIdx.x / kCtasPerHead;          // (sequence, v-head) index
@@ -62,9 +62,9 @@ decode_kernel(const __nv_bfloat16 *__restrict__ q, const __nv_bfloat16 *__restri
     const int row0 = row_block * kRowsPerCta + (threadIdx.x >> 3);
 
     const float exp_A = expf(load_scalar(A_log, h, param_dtype));
-    const float alpha = expf(log_decay(exp_A, load_scalar(a, bh, gate_dtype),
+    const float alpha = expf(log_decay(exp_A, load_scalar(a, bidx * sa + h, gate_dtype),
                                        load_scalar(dt_bias, h, param_dtype)));
-    const float beta = sigmoid_f(load_scalar(b, bh, gate_dtype));
+    const float beta = sigmoid_f(load_scalar(b, bidx * sb + h, gate_dtype));
 
     // This lane's 16 columns of k and q.
     float kf[16], qf[16];
@@ -154,7 +154,9 @@ cudaError_t launch_decode(const DecodeArgs &p, cudaStream_t stream) {
     auto kernel = rows_per_thread == 2 ? (p.qk_l2norm ? decode_kernel<2, true> : decode_kernel<2, false>)
                                        : (p.qk_l2norm ? decode_kernel<1, true> : decode_kernel<1, false>);
     kernel<<<grid, kDecodeThreads, 0, stream>>>(q, k, v, p.state, p.A_log, p.a, p.dt_bias, p.b, p.Hq, p.Hv,
-                                                p.scale, p.gate_dtype, p.param_dtype, o, p.new_state);
+                                                p.scale, p.gate_dtype, p.param_dtype, o, p.new_state,
+                                                static_cast<int>(p.a_stride ? p.a_stride : p.Hv),
+                                                static_cast<int>(p.b_stride ? p.b_stride : p.Hv));
     return cudaGetLastError();
 }
 

@@ -19,6 +19,9 @@ struct DecodeArgs {
     void *out;                   // bf16 [B, Hv, D]
     float *new_state;            // may equal state
     int qk_l2norm;               // 1: q, k <- bf16(x / sqrt(sum x^2 + 1e-6)) inside the kernel
+    // Elements between the gate inputs of consecutive sequences in a and b (Hv when packed;
+    // larger for views into a wider projection output).  0: Hv.
+    int64_t a_stride = 0, b_stride = 0;
 };
 
 struct PrefillArgs {
@@ -41,6 +44,9 @@ struct PrefillArgs {
     // The device status word on this device (device_status_word()), where the kernels
     // record a malformed cu_seqlens; nullptr: no check.
     int *status = nullptr;
+    // Elements between the gate inputs of consecutive tokens in a and b (Hv when packed;
+    // larger for views into a wider projection output).  0: Hv.
+    int64_t a_stride = 0, b_stride = 0;
 };
 
 // Set the message gdn_last_error() returns on this thread.

@@ -79,6 +79,7 @@ struct ChunkParams {
     float *new_state;
     int64_t num_seqs;
     int *status;     // device status word (malformed cu_seqlens), or nullptr
+    int sa, sb;      // elements between consecutive tokens' gate inputs in a, b
 };
 
 // Issue the cp.async copies of chunk tokens [t0, t0+64) into stage `st`.
@@ -155,9 +156,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_chunked_mma_kernel(const 
         for (int u = 0; u < 2; ++u) {
             const int i = lane + 32 * u;
             if (i < nvalid) {
-                const int64_t gi = (tbase + i) * p.Hv + h;
-                ga[u] = load_scalar(p.a, gi, p.gate_dtype);
-                gb[u] = load_scalar(p.b, gi, p.gate_dtype);
+                ga[u] = load_scalar(p.a, (tbase + i) * p.sa + h, p.gate_dtype);
+                gb[u] = load_scalar(p.b, (tbase + i) * p.sb + h, p.gate_dtype);
             }
         }
     };
@@ -471,7 +471,8 @@ cudaError_t launch_prefill_chunked(const PrefillArgs &p, cudaStream_t stream) {
     ChunkParams cp{static_cast<const __nv_bfloat16 *>(p.q), static_cast<const __nv_bfloat16 *>(p.k),
                    static_cast<const __nv_bfloat16 *>(p.v), p.state, p.A_log, p.a, p.dt_bias, p.b,
                    p.cu_seqlens, p.total_tokens, p.Hq, p.Hv, p.scale, p.gate_dtype, p.param_dtype,
-                   static_cast<__nv_bfloat16 *>(p.out), p.new_state, p.num_seqs, p.status};
+                   static_cast<__nv_bfloat16 *>(p.out), p.new_state, p.num_seqs, p.status,
+                   static_cast<int>(p.a_stride ? p.a_stride : p.Hv), static_cast<int>(p.b_stride ? p.b_stride : p.Hv)};
     prefill_chunked_mma_kernel<<<static_cast<unsigned>(ctas), kThreads, SMEM_BYTES, stream>>>(cp);
     return cudaGetLastError();
 }

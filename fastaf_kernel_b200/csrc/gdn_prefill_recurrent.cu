@@ -32,7 +32,7 @@ __device__ __forceinline__ void prefetch_block(Prefetch &pf, const __nv_bfloat16
                                                const __nv_bfloat16 *k, const __nv_bfloat16 *v,
                                                const void *a, const void *b, int gate_dtype,
                                                int64_t t0, int64_t t_end, int Hq, int Hv, int hq,
-                                               int h, int row_base) {
+                                               int h, int row_base, int sa, int sb) {
     const int tid = threadIdx.x;
     // k, q: 16 tokens x 16 uint4 each; thread covers 2 uint4 of k and 2 of q.
 #pragma unroll
@@ -56,8 +56,8 @@ __device__ __forceinline__ void prefetch_block(Prefetch &pf, const __nv_bfloat16
     }
     if (tid < kTokBlock) {
         const int64_t t = t0 + tid;
-        pf.a = t < t_end ? load_scalar(a, t * Hv + h, gate_dtype) : 0.0f;
-        pf.b = t < t_end ? load_scalar(b, t * Hv + h, gate_dtype) : 0.0f;
+        pf.a = t < t_end ? load_scalar(a, t * sa + h, gate_dtype) : 0.0f;
+        pf.b = t < t_end ? load_scalar(b, t * sb + h, gate_dtype) : 0.0f;
     }
 }
 
@@ -67,7 +67,8 @@ prefill_recurrent_kernel(const __nv_bfloat16 *__restrict__ q, const __nv_bfloat1
                          const void *A_log, const void *a, const void *dt_bias, const void *b,
                          const int32_t *__restrict__ cu_seqlens, int64_t N, int64_t T, int Hq, int Hv,
                          float scale, int gate_dtype, int param_dtype,
-                         __nv_bfloat16 *__restrict__ out, float *__restrict__ new_state, int *status) {
+                         __nv_bfloat16 *__restrict__ out, float *__restrict__ new_state, int *status,
+                         int sa, int sb) {
     __shared__ __align__(16) float k_s[kTokBlock][2][kHalfPad];
     __shared__ __align__(16) float q_s[kTokBlock][2][kHalfPad];
     __shared__ float v_s[kTokBlock][kRecRows];
@@ -110,7 +111,7 @@ prefill_recurrent_kernel(const __nv_bfloat16 *__restrict__ q, const __nv_bfloat1
     const float dtb = load_scalar(dt_bias, h, param_dtype);
 
     Prefetch pf;
-    prefetch_block(pf, q, k, v, a, b, gate_dtype, s0, s1, Hq, Hv, hq, h, row_base);
+    prefetch_block(pf, q, k, v, a, b, gate_dtype, s0, s1, Hq, Hv, hq, h, row_base, sa, sb);
     for (int64_t t0 = s0; t0 < s1; t0 += kTokBlock) {
         __syncthreads();   // the previous block is no longer being read
 #pragma unroll
@@ -139,7 +140,7 @@ prefill_recurrent_kernel(const __nv_bfloat16 *__restrict__ q, const __nv_bfloat1
         }
         __syncthreads();
         const int64_t nxt = t0 + kTokBlock;
-        if (nxt < s1) prefetch_block(pf, q, k, v, a, b, gate_dtype, nxt, s1, Hq, Hv, hq, h, row_base);
+        if (nxt < s1) prefetch_block(pf, q, k, v, a, b, gate_dtype, nxt, s1, Hq, Hv, hq, h, row_base, sa, sb);
 
         const int ntok = static_cast<int>(s1 - t0 < kTokBlock ? s1 - t0 : kTokBlock);
         for (int tt = 0; tt < ntok; ++tt) {
@@ -186,7 +187,8 @@ cudaError_t launch_prefill_recurrent(const PrefillArgs &p, cudaStream_t stream) 
         static_cast<const __nv_bfloat16 *>(p.q), static_cast<const __nv_bfloat16 *>(p.k),
         static_cast<const __nv_bfloat16 *>(p.v), p.state, p.A_log, p.a, p.dt_bias, p.b,
         p.cu_seqlens, p.num_seqs, p.total_tokens, p.Hq, p.Hv, p.scale, p.gate_dtype, p.param_dtype,
-        static_cast<__nv_bfloat16 *>(p.out), p.new_state, p.status);
+        static_cast<__nv_bfloat16 *>(p.out), p.new_state, p.status,
+        static_cast<int>(p.a_stride ? p.a_stride : p.Hv), static_cast<int>(p.b_stride ? p.b_stride : p.Hv));
     return cudaGetLastError();
 }
 

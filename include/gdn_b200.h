@@ -112,6 +112,23 @@ GDN_API int gdn_prefill_flags(const void *q, const void *k, const void *v, const
                       int method, int flags, void *stream);
 
 /*
+ * gdn_prefill_flags with the gate inputs a and b read straight from a wider tensor, such
+ * as the output of the projection GEMM that produces them (a Gated DeltaNet layer's fused
+ * projection emits [T, ...] rows holding a and b side by side): token t's gate inputs for
+ * v-head h are a[t * a_row_stride + h] and b[t * b_row_stride + h].  Row strides are in
+ * elements; 0 means num_v_heads (packed [T, Hv]), otherwise they must be >= num_v_heads.
+ * No copy of a or b is made.  No counterpart in the reference (its entry points take
+ * packed tensors and make them contiguous, solution/triton/kernel.py:452-453).
+ */
+GDN_API int gdn_prefill_strided(const void *q, const void *k, const void *v, const float *state,
+                        const void *A_log, const void *a, const void *dt_bias, const void *b,
+                        const int32_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
+                        int num_qk_heads, int num_v_heads, int head_size, float scale,
+                        int gate_dtype, int param_dtype, void *output, float *new_state,
+                        int64_t a_row_stride, int64_t b_row_stride, int method, int flags,
+                        void *stream);
+
+/*
  * gdn_prefill_ex with a caller-provided workspace (no allocation inside the call).
  *
  * The GDN_PREFILL_TCGEN05 kernel computes each chunk's gates and T = (I + A)^-1 for
@@ -231,6 +248,16 @@ GDN_API int gdn_decode_flags(const void *q, const void *k, const void *v, const 
                      int64_t batch, int num_qk_heads, int num_v_heads, int head_size,
                      float scale, int gate_dtype, int param_dtype, void *output,
                      float *new_state, int flags, void *stream);
+
+/* gdn_decode_flags with the gate inputs read as a[s * a_row_stride + h], b[s * b_row_stride
+ * + h] for sequence s (elements; 0 = num_v_heads; otherwise >= num_v_heads), straight from a
+ * wider projection output, without a copy.  No counterpart in the reference. */
+GDN_API int gdn_decode_strided(const void *q, const void *k, const void *v, const float *state,
+                       const void *A_log, const void *a, const void *dt_bias, const void *b,
+                       int64_t batch, int num_qk_heads, int num_v_heads, int head_size,
+                       float scale, int gate_dtype, int param_dtype, void *output,
+                       float *new_state, int64_t a_row_stride, int64_t b_row_stride, int flags,
+                       void *stream);
 
 /*
  * Synchronizes `stream` and reports the library's device status word since the last
