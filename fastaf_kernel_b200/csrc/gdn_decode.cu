@@ -44,8 +44,11 @@ __device__ __forceinline__ void l2norm_8lanes(float (&x)[16]) {
 constexpr int kDecodeThreads = 256;            // 32 rows per pass (8 lanes per row)
 constexpr int kRowsPerPass = kDecodeThreads / 8;
 
+// Three CTAs (24 warps) per SM keep enough loads in flight to stream the state at the
+// HBM rate: the two-rows-per-thread instance must fit 85 registers (at 86 it drops to
+// two CTAs per SM and the B = 512 step is 16 % slower).
 template <int ROWS_PER_THREAD, bool QK_L2NORM>
-__global__ void __launch_bounds__(kDecodeThreads)
+__global__ void __launch_bounds__(kDecodeThreads, 3)
 decode_kernel(const __nv_bfloat16 *__restrict__ q, const __nv_bfloat16 *__restrict__ k,
               const __nv_bfloat16 *__restrict__ v, const float *state, const void *A_log,
               const void *a, const void *dt_bias, const void *b, int Hq, int Hv, float scale,
