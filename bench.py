@@ -21,6 +21,10 @@ heads are independent; the only collectives are the timing barrier and max):
     whole job's prefill tokens/s and decode sequence-steps/s and the load imbalance.
 Timing is device time (CUDA events), max over ranks.
 
+``--small-configs`` times only the two small configurations (a B = 4 decode step and a
+4-sequence varlen prefill) through this library, the reference's Triton kernels and its
+CPU torch code, as eager calls and as CUDA-graph replays (one GPU, one JSON object).
+
 ``--impl reference`` times the reference's own CPU implementation of the path
 (the fp32 torch recurrence of solution/gdn_baseline_torch.py, restated in
 oracle/gdn_ref.py) on the host cores, rank 0 only, on a bounded sample.
@@ -409,6 +413,101 @@ def run_mixed(args, rank, world, dev, barrier, gather, peaks):
     }
 
 
+def _time_calls(fn, calls=200, graph_calls=20, replays=10):
+    """(ms per eager call, device ms per call from replays of a CUDA graph of `graph_calls`
+    calls): the first includes the host cost of each call, the second only the device's."""
+    for _ in range(20):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(calls):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    eager = e0.elapsed_time(e1) / calls
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        fn()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=side):
+            for _ in range(graph_calls):
+                fn()
+    torch.cuda.synchronize()
+    graph.replay()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(replays):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    dev_ms = e0.elapsed_time(e1) / (replays * graph_calls)
+    del graph
+    return eager, dev_ms
+
+
+def run_small_configs(args):
+    """The two small configurations, one GPU: one B = 4 decode step (Hq 16, Hv 32, with
+    state) and a varlen prefill of 4 sequences with lengths U[64, 512] (seed 1: 1,311
+    tokens; sequences 1 and 3 with state).  Each through this library, through the
+    reference's own Triton kernels compiled for sm_100 (oracle/ref_triton.py, when built)
+    and through the reference's CPU torch implementation (oracle/gdn_ref.py) on all host
+    threads.  Prints one JSON object."""
+    import fastaf_kernel_b200 as fk
+    from fastaf_kernel_b200 import workloads as W
+    from oracle import gdn_ref, ref_triton
+    torch.set_num_threads(os.cpu_count() or 1)
+    dev = torch.device("cuda", 0)
+    ref = ref_triton.RefTriton() if ref_triton.available() else None
+    res = {"configs": "small", "cpu_threads": torch.get_num_threads(),
+           "timing": "eager: CUDA events around 200 calls; graph: replays of a CUDA graph of 20 calls"}
+    # decode, B = 4
+    d = W.decode_inputs(4, seed=0)
+    g = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in d.items()}
+    out = torch.empty((4, 1, 32, 128), dtype=torch.bfloat16, device=dev)
+    ns = torch.empty_like(g["state"])
+    nbytes = 4 * W.bytes_per_decode_seq()
+    ours = _time_calls(lambda: fk.kernel_decode(g["q"], g["k"], g["v"], g["state"], g["A_log"], g["a"],
+                                                g["dt_bias"], g["b"], g["scale"], output=out, new_state=ns))
+    dec = {"workload": "gdn_decode_b4_hq16_hv32_d128", "bytes_per_step": nbytes,
+           "ours_ms": {"eager": ours[0], "graph": ours[1]}, "ours_gbs": nbytes / (ours[1] / 1e3) / 1e9}
+    if ref is not None:
+        o2 = out.view(4, 32, 128)
+        rt = _time_calls(lambda: ref.decode(g["q"], g["k"], g["v"], g["state"], g["A_log"], g["a"],
+                                            g["dt_bias"], g["b"], g["scale"], o2, ns))
+        dec["ref_triton_ms"] = {"eager": rt[0], "graph": rt[1]}
+    t0 = time.perf_counter()
+    for _ in range(5):
+        gdn_ref.decode(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"], d["dt_bias"], d["b"], d["scale"])
+    dec["cpu_torch_ms"] = (time.perf_counter() - t0) / 5 * 1e3
+    res["decode_b4"] = dec
+    # varlen prefill, 4 sequences U[64, 512]
+    x = W.prefill_varlen(seed=1)
+    T = x["q"].shape[0]
+    g = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in x.items()}
+    out = torch.empty((T, 32, 128), dtype=torch.bfloat16, device=dev)
+    ns = torch.empty((4, 32, 128, 128), device=dev)
+    ours = _time_calls(lambda: fk.kernel(g["q"], g["k"], g["v"], g["state"], g["A_log"], g["a"], g["dt_bias"],
+                                         g["b"], g["cu_seqlens"], g["scale"], output=out, new_state=ns))
+    pre = {"workload": f"gdn_prefill_varlen_4seqs_{T}tok_hq16_hv32_d128", "tokens": T,
+           "method": fk.prefill_method(T, num_seqs=4), "ours_ms": {"eager": ours[0], "graph": ours[1]},
+           "ours_tokens_per_s": T / (ours[1] / 1e3)}
+    if ref is not None:
+        rt = _time_calls(lambda: ref.prefill(g["q"], g["k"], g["v"], g["state"], g["A_log"], g["a"],
+                                             g["dt_bias"], g["b"], g["cu_seqlens"], g["scale"], out, ns),
+                         calls=50)
+        pre["ref_triton_ms"] = {"eager": rt[0], "graph": rt[1]}
+    t0 = time.perf_counter()
+    gdn_ref.prefill(x["q"], x["k"], x["v"], x["state"], x["A_log"], x["a"], x["dt_bias"], x["b"],
+                    x["cu_seqlens"], x["scale"])
+    pre["cpu_torch_ms"] = (time.perf_counter() - t0) * 1e3
+    res["prefill_varlen"] = pre
+    print(json.dumps(res))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -424,11 +523,15 @@ def main():
     ap.add_argument("--no-cp", action="store_true", help="skip the context-parallel prefill (N > 1)")
     ap.add_argument("--no-ref-gpu", action="store_true",
                     help="skip timing the reference's own Triton kernels on this GPU")
+    ap.add_argument("--small-configs", action="store_true",
+                    help="time only the B = 4 decode step and the 4-sequence varlen prefill (one GPU)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.impl == "reference":
         return reference_arm(args)
+    if args.small_configs:
+        return run_small_configs(args)
 
     import torch.distributed as dist
     import fastaf_kernel_b200 as fk

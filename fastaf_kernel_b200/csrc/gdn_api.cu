@@ -197,10 +197,12 @@ static int prefill_tc_call(const gdn::PrefillArgs &p, void *workspace, size_t wo
         if (e != cudaSuccess) return cuda_status(e, "gdn_prefill (tcgen05) launch");
         return gate_output(p, s);
     }
+    // The pool block also holds the sequences' launch order (need is a multiple of 256 bytes).
     void *ws = nullptr;
-    cudaError_t e = pool_alloc(&ws, need, s);
+    cudaError_t e = pool_alloc(&ws, need + static_cast<size_t>(p.num_seqs) * sizeof(int32_t), s);
     if (e != cudaSuccess) return cuda_status(e, "gdn_prefill (tcgen05) workspace");
-    e = gdn::launch_prefill_tc(p, ws, s, /*overlap=*/true);
+    e = gdn::launch_prefill_tc(p, ws, s, /*overlap=*/true,
+                               reinterpret_cast<int32_t *>(static_cast<char *>(ws) + need));
     const cudaError_t ef = cudaFreeAsync(ws, s);
     if (e != cudaSuccess) return cuda_status(e, "gdn_prefill (tcgen05) launch");
     if (ef != cudaSuccess) return cuda_status(ef, "gdn_prefill (tcgen05) workspace release");
@@ -374,7 +376,8 @@ int gdn_output_gate(void *output, const void *gate, const void *weight, int weig
 int gdn_prefill_tc_launches(int64_t num_seqs, int num_qk_heads, int num_v_heads, int num_sms) {
     if (num_seqs <= 0 || num_qk_heads <= 0 || num_v_heads <= 0 || num_v_heads % num_qk_heads != 0) return 0;
     const int nh = ((num_v_heads / num_qk_heads) % 2 == 0) ? 2 : 1;
-    return gdn::prefill_tc_overlap_tail(num_seqs * num_v_heads, num_sms, nh) > 0 ? 4 : 2;
+    return (gdn::prefill_tc_overlap_tail(num_seqs * num_v_heads, num_sms, nh) > 0 ? 4 : 2) +
+           (gdn::prefill_tc_orders_chains(num_seqs, num_v_heads, num_sms) ? 1 : 0);
 }
 
 int gdn_prefill_resolve(int64_t total_tokens, int64_t num_seqs, int method) {

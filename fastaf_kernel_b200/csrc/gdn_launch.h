@@ -70,7 +70,21 @@ bool prefill_chunked_supported(const PrefillArgs &p);
 // chain kernels -- on a library-owned high-priority stream, the rest on `stream`, so the
 // short group's chains run while the rest is being prepped (fork and join through
 // events; same kernels, same results).
-cudaError_t launch_prefill_tc(const PrefillArgs &p, void *workspace, cudaStream_t stream, bool overlap = false);
+// With `order` (room for num_seqs int32), a call of more chains than SMs first ranks its
+// sequences longest first on the device (launch_chain_order) and the chain kernel takes
+// them in that order, so the block scheduler starts the longest chains first.  Only the
+// sequences whose chains all stay on `stream` are ranked; the chunk prep, which finishes
+// before the chains on its stream start, covers the same sequences in index order.
+cudaError_t launch_prefill_tc(const PrefillArgs &p, void *workspace, cudaStream_t stream, bool overlap = false,
+                              int32_t *order = nullptr);
+// order[r] for r < ranked = the sequence of rank r among sequences [0, ranked), ranked by
+// clamped length, longest first, ties by index; order[r] = r for ranked <= r < num_seqs.
+// A permutation of [0, num_seqs) whatever cu_seqlens holds.
+cudaError_t launch_chain_order(const int32_t *cu_seqlens, int64_t num_seqs, int64_t ranked,
+                               int64_t total_tokens, int32_t *order, cudaStream_t stream);
+// Whether launch_prefill_tc ranks the sequences of a call (more than one sequence and
+// more chains than the device's SMs).
+bool prefill_tc_orders_chains(int64_t num_seqs, int Hv, int sms);
 // Chains launch_prefill_tc puts on the overlap stream for `chains` chains on `sms` SMs
 // (0: no split): chains mod sms when there are more chains than SMs and that tail is a
 // whole number of prep CTAs (heads_per_prep_cta v-heads each).

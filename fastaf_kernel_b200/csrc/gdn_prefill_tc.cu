@@ -18,7 +18,8 @@
 // partial chunk have beta = 0 and log alpha = 0.  Every product with an fp32 operand
 // (S0, T, W, the decayed delta) splits it into bf16 hi + lo.
 //
-// One CTA per (sequence, v-head) chain, 14 warps in four roles that hand chunks to
+// One CTA per (sequence, v-head) chain (the pooled entry points may rank the sequences
+// longest first, TcParams::order), 14 warps in four roles that hand chunks to
 // each other through mbarriers, so the next chunk's state-independent products run
 // while the current chunk's state update is on the tensor core:
 //   warp 0      allocates all 512 TMEM columns; lane 0 issues every MMA, each batch as
@@ -120,8 +121,9 @@ struct TcParams {
     const uint8_t *ws_T;
     const float *ws_g;
     const __nv_bfloat16 *ws_P;
-    int64_t chain0;   // (sequence, v-head) chain of blockIdx.x = 0
+    int64_t chain0;   // (sequence rank, v-head) chain of blockIdx.x = 0
     uint64_t wait_ns; // limit of every role's wait (ns)
+    const int32_t *order;   // sequence of each rank (nullptr: rank = sequence index)
 };
 
 struct Bars {
@@ -199,9 +201,11 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t lane_base = static_cast<uint32_t>(warp & 3) * 32;
     const int row = static_cast<int>(lane_base) + lane;    // this thread's TMEM lane (warps 1-8)
-    const int64_t chain = blockIdx.x + p.chain0;
-    const int64_t n = chain / p.Hv;
+    const int64_t chain = blockIdx.x + p.chain0;           // (sequence rank, v-head)
+    const int64_t rank = chain / p.Hv;
+    const int64_t n = p.order ? p.order[rank] : rank;
     const int h = static_cast<int>(chain % p.Hv);
+    const int64_t nh = n * p.Hv + h;                         // (sequence, v-head) of the state
     const int hq = h / (p.Hv / p.Hq);
     if (tid == 0 && h == 0) check_seq_bounds(p.cu_seqlens, n, p.num_seqs, p.T, &g_tc_error);
     int64_t s0 = p.cu_seqlens[n], s1 = p.cu_seqlens[n + 1];
@@ -221,7 +225,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
     // the four prep warps' hand-offs around the output staging tile (two per output chunk)
     const uint32_t b_stg = smem_u32(&bars.stg);
     const uint64_t wl = p.wait_ns;
-    float *dst_state = p.new_state + chain * kHeadDim * kHeadDim;
+    float *dst_state = p.new_state + nh * kHeadDim * kHeadDim;
 
     if (warp == 0) {
         if (lane == 0) {
@@ -546,7 +550,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         const int v = row;    // state row / token row of this thread's TMEM lane
         const int hs = (warp - 5) >> 2;
         {
-            const float *src = p.state ? p.state + (chain * kHeadDim + v) * kHeadDim : nullptr;
+            const float *src = p.state ? p.state + (nh * kHeadDim + v) * kHeadDim : nullptr;
 #pragma unroll 1
             for (int q4 = 2 * hs; q4 < 2 * hs + 2; ++q4) {
                 uint32_t r[32];
@@ -673,6 +677,68 @@ size_t prefill_tc_workspace_bytes(const PrefillArgs &p) {
     return static_cast<size_t>(tc_workspace_bytes(p.total_tokens, p.num_seqs, p.Hv));
 }
 
+namespace {
+
+// order[r] = the sequence of rank r among sequences [0, R) (longest first, ties by
+// index), order[r] = r for R <= r < N.  One thread per sequence i, 32 per CTA; the CTA's
+// eight warps split the sequences j it is compared with, 32 at a time (one load per
+// lane, then a broadcast per j), and add their counts.  The rank of i is the number of
+// j that come before it, so ranks are distinct.
+constexpr int kOrderWarps = 8;
+
+__device__ __forceinline__ int clamped_length(const int32_t *cu, int64_t j, int64_t T) {
+    int64_t s0 = cu[j], s1 = cu[j + 1];
+    s0 = s0 < 0 ? 0 : (s0 > T ? T : s0);
+    s1 = s1 < s0 ? s0 : (s1 > T ? T : s1);
+    return static_cast<int>(s1 - s0);
+}
+
+__global__ void __launch_bounds__(32 * kOrderWarps)
+chain_order_kernel(const int32_t *cu, int64_t N, int64_t R, int64_t T, int32_t *order) {
+    __shared__ int counts[kOrderWarps][32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * 32 + lane;
+    // Every lane runs the whole loop (full-warp shuffles, one block barrier); a lane
+    // past R counts against length -2, which no sequence has, and its count is unused.
+    const int li = i < R ? clamped_length(cu, i, T) : -2;
+    int before = 0;
+    for (int64_t jb = static_cast<int64_t>(warp) * 32; jb < R; jb += 32 * kOrderWarps) {
+        const int lj_own = jb + lane < R ? clamped_length(cu, jb + lane, T) : -1;   // -1: no sequence
+#pragma unroll 8
+        for (int jj = 0; jj < 32; ++jj) {
+            const int lj = __shfl_sync(0xffffffffu, lj_own, jj);
+            before += (lj > li) || (lj == li && jb + jj < i);
+        }
+    }
+    counts[warp][lane] = before;
+    __syncthreads();
+    if (warp == 0 && i < R) {
+        int r = 0;
+#pragma unroll
+        for (int w = 0; w < kOrderWarps; ++w) r += counts[w][lane];
+        order[r] = static_cast<int32_t>(i);
+    } else if (warp == 0 && i < N) {
+        order[i] = static_cast<int32_t>(i);
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_chain_order(const int32_t *cu_seqlens, int64_t num_seqs, int64_t ranked,
+                               int64_t total_tokens, int32_t *order, cudaStream_t stream) {
+    if (num_seqs <= 0) return cudaSuccess;
+    if (ranked < 0 || ranked > num_seqs) return cudaErrorInvalidValue;
+    const int64_t ctas = (num_seqs + 31) / 32;
+    if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+    chain_order_kernel<<<static_cast<unsigned>(ctas), 32 * kOrderWarps, 0, stream>>>(
+        cu_seqlens, num_seqs, ranked, total_tokens, order);
+    return cudaGetLastError();
+}
+
+bool prefill_tc_orders_chains(int64_t num_seqs, int Hv, int sms) {
+    return num_seqs >= 2 && sms > 0 && num_seqs * Hv > sms;
+}
+
 int64_t prefill_tc_overlap_tail(int64_t chains, int sms, int heads_per_prep_cta) {
     if (sms <= 0 || chains <= sms) return 0;
     const int64_t tail = chains % sms;
@@ -751,7 +817,8 @@ bool aux_usable(cudaStream_t stream, cudaStream_t aux) {
 // and the long group's chains fill whole waves.  The chain kernel takes one SM per chain
 // (all 512 TMEM columns), so without the split the last wave of a batch of equal-length
 // chains leaves (SMs - chains mod SMs) SMs idle for a whole chain length.
-cudaError_t launch_prefill_tc(const PrefillArgs &p, void *workspace, cudaStream_t stream, bool overlap) {
+cudaError_t launch_prefill_tc(const PrefillArgs &p, void *workspace, cudaStream_t stream, bool overlap,
+                              int32_t *order) {
     const int64_t ctas = p.num_seqs * p.Hv;
     if (ctas == 0) return cudaSuccess;
     if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
@@ -772,29 +839,52 @@ cudaError_t launch_prefill_tc(const PrefillArgs &p, void *workspace, cudaStream_
     if (e != cudaSuccess) return e;
     const uint64_t limit = g_wait_limit_ns.load(std::memory_order_relaxed);
     const uint64_t wait_ns = limit ? limit : kDefaultWaitNs;
+    // The split: the last `tail` chains (0: none) on the overlap stream.
+    std::unique_lock<std::mutex> lock(g_overlap_mu, std::defer_lock);
+    OverlapStream *o = nullptr;
+    int64_t tail = 0;
+    if (overlap) {
+        lock.lock();
+        o = overlap_stream(stream);
+        if (o && aux_usable(stream, o->aux)) tail = prefill_tc_overlap_tail(ctas, o->sms, prep_heads_per_cta(p));
+    }
+    if (order) {
+        // Chains run in launch order as SMs free up (list scheduling); longest first keeps
+        // a long sequence late in the batch from starting its chains last.  Ranked: the
+        // sequences whose chains all run on `stream` (the chunk prep there covers the same
+        // sequences, in index order, before those chains start); the others keep their place.
+        int sms = o ? o->sms : 0;
+        if (!o) {
+            int dev = 0;
+            if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+            if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+        }
+        if (prefill_tc_orders_chains(p.num_seqs, p.Hv, sms)) {
+            const int64_t ranked = (ctas - tail) / p.Hv;
+            if ((e = launch_chain_order(p.cu_seqlens, p.num_seqs, ranked, p.total_tokens, order, stream)) !=
+                cudaSuccess)
+                return e;
+        } else {
+            order = nullptr;
+        }
+    }
     // prep + chains of [c0, c1) on stream st
     auto launch_range = [&](int64_t c0, int64_t c1, cudaStream_t st) -> cudaError_t {
         cudaError_t er = launch_chunk_prep(p, ws_T, ws_P, ws_g, st, c0, c1);
         if (er != cudaSuccess) return er;
         TcParams tp{p.state, p.cu_seqlens, p.num_seqs, p.total_tokens, p.Hq, p.Hv, p.scale,
-                    static_cast<__nv_bfloat16 *>(p.out), p.new_state, ws_T, ws_g, ws_P, c0, wait_ns};
+                    static_cast<__nv_bfloat16 *>(p.out), p.new_state, ws_T, ws_g, ws_P, c0, wait_ns, order};
         prefill_tc_kernel<<<static_cast<unsigned>(c1 - c0), kThreads, SMEM_BYTES, st>>>(qm, km, vm, tp);
         return cudaGetLastError();
     };
-    if (overlap) {
-        std::lock_guard<std::mutex> lock(g_overlap_mu);
-        OverlapStream *o = overlap_stream(stream);
-        if (o && aux_usable(stream, o->aux)) {
-            const int64_t tail = prefill_tc_overlap_tail(ctas, o->sms, prep_heads_per_cta(p));
-            if (tail > 0) {
-                if ((e = cudaEventRecord(o->fork, stream)) != cudaSuccess) return e;
-                if ((e = cudaStreamWaitEvent(o->aux, o->fork, 0)) != cudaSuccess) return e;
-                if ((e = launch_range(ctas - tail, ctas, o->aux)) != cudaSuccess) return e;
-                if ((e = cudaEventRecord(o->join, o->aux)) != cudaSuccess) return e;
-                if ((e = launch_range(0, ctas - tail, stream)) != cudaSuccess) return e;
-                return cudaStreamWaitEvent(stream, o->join, 0);
-            }
-        }
+    if (tail > 0) {
+        // (the order kernel above is on `stream` before the fork)
+        if ((e = cudaEventRecord(o->fork, stream)) != cudaSuccess) return e;
+        if ((e = cudaStreamWaitEvent(o->aux, o->fork, 0)) != cudaSuccess) return e;
+        if ((e = launch_range(ctas - tail, ctas, o->aux)) != cudaSuccess) return e;
+        if ((e = cudaEventRecord(o->join, o->aux)) != cudaSuccess) return e;
+        if ((e = launch_range(0, ctas - tail, stream)) != cudaSuccess) return e;
+        return cudaStreamWaitEvent(stream, o->join, 0);
     }
     return launch_range(0, ctas, stream);
 }

@@ -137,6 +137,9 @@ GDN_API int gdn_prefill_strided(const void *q, const void *k, const void *v, con
  * this entry point takes it from the caller.  `workspace` must be 256-byte aligned
  * and hold gdn_prefill_workspace_size() bytes; other methods ignore it.  The
  * workspace must not be reused by other work until the call's stream reaches it.
+ * The chains run on the caller's stream alone and in sequence order (the pooled entry
+ * points may split off the last partial wave onto a second stream and rank the
+ * sequences longest first; the results are the same bits).
  * No counterpart in the reference (its Triton kernel keeps no workspace).
  */
 GDN_API int gdn_prefill_ws(const void *q, const void *k, const void *v, const float *state,
@@ -204,11 +207,14 @@ GDN_API int gdn_prefill_gated(const void *q, const void *k, const void *v, const
 GDN_API int gdn_prefill_resolve(int64_t total_tokens, int64_t num_seqs, int method);
 
 /* Kernel launches of one tcgen05 prefill through the pooled-workspace entry points
- * (gdn_prefill, gdn_prefill_ex, gdn_prefill_flags, gdn_prefill_gated without its gating
- * pass) on a device with `num_sms` SMs: 2 (chunk prep, chains), or 4 when the last
- * partial wave of (sequence, v-head) chains is split onto the library's second stream
- * (more chains than SMs, chains mod SMs > 0 and a whole number of prep CTAs); 0 for
- * invalid shapes.  Host arithmetic only.  No counterpart in the reference. */
+ * (gdn_prefill, gdn_prefill_ex, gdn_prefill_flags, gdn_prefill_strided, gdn_prefill_gated
+ * without its gating pass) on a device with `num_sms` SMs: 2 (chunk prep, chains), or 4
+ * when the last partial wave of (sequence, v-head) chains is split onto the library's
+ * second stream (more chains than SMs, chains mod SMs > 0 and a whole number of prep
+ * CTAs); plus 1 when there are at least 2 sequences and more chains than SMs: a kernel
+ * that ranks the sequences longest first on the device, so the chains of the longest
+ * sequences start first (the results do not depend on the order).  0 for invalid
+ * shapes.  Host arithmetic only.  No counterpart in the reference. */
 GDN_API int gdn_prefill_tc_launches(int64_t num_seqs, int num_qk_heads, int num_v_heads, int num_sms);
 
 /* Workspace bytes gdn_prefill_ws needs for GDN_PREFILL_TCGEN05:

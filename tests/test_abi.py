@@ -105,13 +105,16 @@ def test_error_maps_to_python_exceptions():
 
 
 @pytest.mark.parametrize("n,hq,hv,sms,launches", [
-    (16, 16, 32, 148, 4),    # 512 chains: the last 68 go to the second stream
-    (4, 16, 32, 148, 2),     # fewer chains than SMs
-    (37, 2, 4, 148, 2),      # 148 chains: whole waves, no split
-    (13, 4, 12, 148, 4),     # one v-head per prep CTA: tail of 8
-    (16, 16, 32, 147, 2),    # a tail of 71 is not a whole number of two-head prep CTAs
+    (16, 16, 32, 148, 5),    # 512 chains: the last 68 go to the second stream; sequences ranked
+    (4, 16, 32, 148, 2),     # fewer chains than SMs: no split, no ranking
+    (37, 2, 4, 148, 2),      # 148 chains: whole waves, no split, not more chains than SMs
+    (74, 2, 4, 148, 3),      # 296 chains: whole waves, no split; sequences ranked
+    (13, 4, 12, 148, 5),     # one v-head per prep CTA: tail of 8; sequences ranked
+    (16, 16, 32, 147, 3),    # a tail of 71 is not a whole number of two-head prep CTAs
+    (1, 4, 512, 148, 4),     # one sequence of 512 chains: a tail of 68 split off, nothing to rank
     (1, 3, 4, 148, 0),       # invalid head counts
 ])
 def test_prefill_tc_launch_count_rule(n, hq, hv, sms, launches):
-    """The host query of the tcgen05 prefill's launch count (the wave-split rule)."""
+    """The host query of the tcgen05 prefill's launch count: the wave-split rule, plus
+    the ranking of the sequences when there are several and more chains than SMs."""
     assert _lib.load().gdn_prefill_tc_launches(n, hq, hv, sms) == launches

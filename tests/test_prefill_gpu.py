@@ -306,6 +306,32 @@ def test_prefill_tc_wave_split_matches_single_stream(lengths, Hq, Hv):
     assert_parity(o.cpu(), ro, s.cpu(), rs)
 
 
+@pytest.mark.parametrize("n_seqs,Hq,Hv,seed", [
+    (37, 4, 8, 61),      # 296 chains = 2 x 148: every sequence ranked, no split
+    (300, 4, 8, 62),     # 2400 chains: split tail of 32 chains, the other 296 sequences ranked
+])
+def test_prefill_tc_longest_first_order_matches_index_order(n_seqs, Hq, Hv, seed):
+    """Shuffled lengths (empty, one-token, chunk-boundary and long sequences): the pooled call
+    ranks the sequences longest first on the device before its chains; the result is bit for
+    bit that of the caller-workspace call, whose chains run in sequence order on one stream,
+    and within tolerance of the oracle."""
+    sms = torch.cuda.get_device_properties(DEV).multi_processor_count
+    assert n_seqs * Hv > sms
+    rng = np.random.default_rng(seed)
+    lengths = [int(v) for v in rng.integers(0, 400, size=n_seqs)]
+    lengths[:6] = [0, 1, 64, 65, 128, 0]
+    rng.shuffle(lengths)
+    x = W.prefill_inputs(lengths, seed=seed, Hq=Hq, Hv=Hv)
+    g = _gpu(x)
+    o, s = fk.kernel(g["q"], g["k"], g["v"], g["state"], g["A_log"], g["a"], g["dt_bias"], g["b"],
+                     g["cu_seqlens"], g["scale"], method="tcgen05")
+    o1, s1 = _ws_call(g, n_seqs, Hq, Hv)
+    fk.device_status()
+    assert torch.equal(o, o1) and torch.equal(s, s1)
+    ro, rs = _oracle(x)
+    assert_parity(o.cpu(), ro, s.cpu(), rs)
+
+
 def test_prefill_tc_wave_split_under_graph_capture():
     """The split launch (fork onto the library's second stream, join back) records into a
     CUDA graph, and replaying it reproduces the eager result."""
@@ -364,7 +390,8 @@ def test_prefill_tc_eager_call_during_a_capture_that_holds_the_split():
 @pytest.mark.parametrize("n_seqs", [3, 16])
 def test_prefill_tc_launch_count_matches_query(n_seqs):
     """The kernels one pooled tcgen05 call launches (counted by the profiler) are what
-    gdn_prefill_tc_launches reports: 2 below the wave-split threshold, 4 above it."""
+    gdn_prefill_tc_launches reports: 2 below the wave-split threshold; above it 4, plus the
+    kernel that ranks the sequences longest first."""
     from torch.profiler import ProfilerActivity, profile
     from fastaf_kernel_b200 import _lib
     x = W.prefill_inputs([128] * n_seqs, seed=35)
@@ -377,6 +404,6 @@ def test_prefill_tc_launch_count_matches_query(n_seqs):
         run()
         torch.cuda.synchronize()
     names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
-    ours = [n for n in names if "chunk_prep_kernel" in n or "prefill_tc_kernel" in n]
+    ours = [n for n in names if "chunk_prep_kernel" in n or "prefill_tc_kernel" in n or "chain_order_kernel" in n]
     sms = torch.cuda.get_device_properties(DEV).multi_processor_count
     assert len(ours) == _lib.load().gdn_prefill_tc_launches(n_seqs, 16, 32, sms), names
