@@ -173,9 +173,8 @@ int gdn_decode_strided(const void *q, const void *k, const void *v, const float 
     return cuda_status(gdn::launch_decode(p, static_cast<cudaStream_t>(stream)), "gdn_decode launch");
 }
 
-// The optional gated RMSNorm of the output, as its own pass after the prefill (a
-// version fused into the tcgen05 chains' output store that loaded the gate rows there
-// measured 2x slower: those warps feed the next chunk's delta batch).
+// The optional gated RMSNorm of the output, as its own pass after the prefill kernels
+// that do not fuse it (the tcgen05 chains apply it in their output stores).
 static int gate_output(const gdn::PrefillArgs &p, cudaStream_t s) {
     if (!p.out_gate) return GDN_OK;
     return cuda_status(gdn::launch_output_gate(p.out, p.out_gate, p.norm_w, p.norm_w_dtype,
@@ -193,9 +192,9 @@ static int prefill_tc_call(const gdn::PrefillArgs &p, void *workspace, size_t wo
         if (workspace_bytes < need)
             return fail(GDN_ERR_INVALID_ARGUMENT, "workspace of %zu bytes is smaller than the %zu needed",
                         workspace_bytes, need);
-        const cudaError_t e = gdn::launch_prefill_tc(p, workspace, s);
+        const cudaError_t e = gdn::launch_prefill_tc(p, workspace, s);   // (gating fused into its stores)
         if (e != cudaSuccess) return cuda_status(e, "gdn_prefill (tcgen05) launch");
-        return gate_output(p, s);
+        return GDN_OK;
     }
     // The pool block also holds the sequences' launch order (need is a multiple of 256 bytes).
     void *ws = nullptr;
@@ -206,7 +205,7 @@ static int prefill_tc_call(const gdn::PrefillArgs &p, void *workspace, size_t wo
     const cudaError_t ef = cudaFreeAsync(ws, s);
     if (e != cudaSuccess) return cuda_status(e, "gdn_prefill (tcgen05) launch");
     if (ef != cudaSuccess) return cuda_status(ef, "gdn_prefill (tcgen05) workspace release");
-    return gate_output(p, s);
+    return GDN_OK;   // (the chains' stores applied the gating)
 }
 
 static int prefill_impl(const void *q, const void *k, const void *v, const float *state,

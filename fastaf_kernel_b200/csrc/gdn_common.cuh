@@ -64,7 +64,11 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 // Gated RMSNorm of one 128-element bf16 vector held by an aligned group of 16 lanes,
 // 8 elements (one 16-byte word) each: o / sqrt(mean(o^2) + eps) * w * silu(z), fp32,
 // rounded to bf16.  ow / zw are this lane's words of o and z, wv its 8 weights.  Every
-// lane of the warp must call it (full-warp shuffles).
+// lane of the warp must call it (full-warp shuffles).  The reciprocal square root, the
+// exponential and the division of silu use the hardware approximations (rsqrtf, __expf,
+// __fdividef: a few ulp in fp32, far below the bf16 rounding of the result), so the
+// tcgen05 prefill's output-store warps keep up with a chunk in their shared budget; the
+// standalone pass uses this same routine, so both give the same bits.
 __device__ __forceinline__ uint4 gated_rmsnorm16(uint4 ov, uint4 zv, const float (&wv)[8], float eps) {
     const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w}, zw[4] = {zv.x, zv.y, zv.z, zv.w};
     float x[8], g[8];
@@ -78,7 +82,7 @@ __device__ __forceinline__ uint4 gated_rmsnorm16(uint4 ov, uint4 zv, const float
     for (int e = 0; e < 8; ++e) ss = fmaf(x[e], x[e], ss);
 #pragma unroll
     for (int m = 1; m < 16; m <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
-    const float inv = 1.0f / sqrtf(ss * (1.0f / 128.0f) + eps);
+    const float inv = rsqrtf(ss * (1.0f / 128.0f) + eps);
     uint32_t r[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -86,7 +90,7 @@ __device__ __forceinline__ uint4 gated_rmsnorm16(uint4 ov, uint4 zv, const float
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
             const int i = 2 * e + u;
-            y[u] = x[i] * inv * wv[i] * (g[i] / (1.0f + expf(-g[i])));
+            y[u] = x[i] * inv * wv[i] * __fdividef(g[i], 1.0f + __expf(-g[i]));
         }
         r[e] = pack_bf16x2(y[0], y[1]);
     }

@@ -70,6 +70,8 @@ bool prefill_chunked_supported(const PrefillArgs &p);
 // chain kernels -- on a library-owned high-priority stream, the rest on `stream`, so the
 // short group's chains run while the rest is being prepped (fork and join through
 // events; same kernels, same results).
+// With p.out_gate set, the chains' output stores apply the gated RMSNorm themselves (the
+// result equals the prefill followed by launch_output_gate bit for bit).
 // With `order` (room for num_seqs int32), a call of more chains than SMs first ranks its
 // sequences longest first on the device (launch_chain_order) and the chain kernel takes
 // them in that order, so the block scheduler starts the longest chains first.  Only the

@@ -19,7 +19,7 @@
 // (S0, T, W, the decayed delta) splits it into bf16 hi + lo.
 //
 // One CTA per (sequence, v-head) chain (the pooled entry points may rank the sequences
-// longest first, TcParams::order), 14 warps in four roles that hand chunks to
+// longest first, TcParams::order), 16 warps in five roles that hand chunks to
 // each other through mbarriers, so the next chunk's state-independent products run
 // while the current chunk's state update is on the tensor core:
 //   warp 0      allocates all 512 TMEM columns; lane 0 issues every MMA, each batch as
@@ -29,7 +29,10 @@
 //   warp 13     lane 0 issues the copies of each chunk (TMA tiles, bulk T tiles, P and
 //               gates) as soon as their previous readers are done
 //   warps 1-4   prep (one per TMEM lane quadrant): the diag(Gamma) Q tile, -W from W^T
-//               in TMEM, then the previous chunk's output rows from O^T in TMEM
+//               in TMEM, then the previous chunk's output rows from O^T in TMEM into a
+//               bf16 staging tile
+//   warps 14-17 output stores: the staging tile's rows to global memory, with the gated
+//               RMSNorm of the output applied on the way when the call asks for it
 //   warps 5-12  state path, two halves of four warps: S -> hi/lo split and decay, the
 //               innovation split
 // The fp32 state lives in TMEM columns [0,128) for the whole sequence.  The barrier
@@ -37,10 +40,10 @@
 //
 // Every wait is bounded (2 s by default, TcParams::wait_ns).  A wait that gives up
 // records its site in g_tc_error and raises a shared abort flag; every role then stops
-// at its next wait (the prep warps' staging hand-off included: it is an mbarrier, not a
-// named barrier, so a warp that stopped cannot leave the others waiting), the issuing
-// thread waits for the last commit of every MMA batch it issued and the copy thread for
-// every copy it issued (both bounded by kDrainWaitNs), and the CTA frees TMEM and exits.
+// at its next wait (the staging-tile hand-off between the prep and store warps included),
+// the issuing thread waits for the last commit of every MMA batch it issued and the copy
+// thread for every copy it issued (both bounded by kDrainWaitNs), and the CTA frees TMEM
+// and exits.
 #include <cuda_bf16.h>
 #include <atomic>
 #include <cstring>
@@ -49,6 +52,7 @@
 #include "gdn_chunk_common.cuh"
 #include "gdn_common.cuh"
 #include "gdn_launch.h"
+#include "gdn_mma_sync.cuh"
 #include "gdn_tc_workspace.h"
 #include "sm100.cuh"
 #include "tma_host.h"
@@ -63,9 +67,16 @@ constexpr uint64_t kDefaultWaitNs = 2000000000ull;
 namespace {
 
 using namespace sm100;
+using msync::cp_async16;
+using msync::cp_async_commit;
+using msync::cp_async_wait;
 
 constexpr int kC = 64;
-constexpr int kThreads = 448;   // warp 0: MMA issue; warps 1-4: prep; warps 5-12: state (two halves); warp 13: copies
+// warp 0: MMA issue; warps 1-4: prep; warps 5-12: state (two halves); warp 13: copies;
+// warps 14-17: output stores (and the gated RMSNorm of the output, when asked for).
+// 576 threads leave at most 112 registers a thread (65,536 per SM, one CTA).
+constexpr int kThreads = 576;
+constexpr int kStoreWarps = 4;
 
 // Shared memory map (bytes from the 1024-aligned dynamic base).
 constexpr uint32_t OFF_KQ = 0;              // 2 stages x 32 KB: [K_h0 | Q_h0 | K_h1 | Q_h1]
@@ -83,6 +94,11 @@ constexpr uint32_t OFF_WL = 176 * 1024;     //   one N = 192 operand of the delt
 constexpr uint32_t OFF_QS = 192 * 1024;
 constexpr uint32_t OFF_GST = 208 * 1024;    // 2 stages x 1 KB: beta, gamma*log2(e), Gamma, decay-to-end
 constexpr uint32_t SMEM_BYTES = 210 * 1024;
+// With the gated output: the store warps' gate rows of one chunk, bf16 [64][128] (16 KB).
+constexpr uint32_t OFF_Z = SMEM_BYTES;
+constexpr uint32_t SMEM_BYTES_GATED = SMEM_BYTES + 16 * 1024;
+constexpr int kStoreWarp0 = 14;
+constexpr int kStoreRows = kC / kStoreWarps;     // rows of an output chunk per store warp
 static_assert(OFF_T1L - OFF_T1H == kTcTileBytes && OFF_T2H - OFF_T1H == 2 * kTcTileBytes,
               "T tiles sit in shared memory in their workspace order (T'_hi rows 0-63 and T'_lo rows"
               " 64-127 of one K-major N = 128 operand)");
@@ -103,7 +119,8 @@ constexpr uint32_t TM_X = 384;    // [384,448) (T'_lo V)^T - S_hi W_lo^T
 constexpr uint32_t TM_O = 448;    // [448,512) (Gamma Q S_hi^T)^T, then O^T (zero before the batch)
 
 enum WaitSite { kWaitTma = 1, kWaitWU = 3, kWaitD = 4, kWaitS = 5, kWaitTT = 6,
-                kWaitW = 7, kWaitSS = 8, kWaitDS = 9, kWaitT = 10, kWaitIssue = 11, kWaitUD = 12 };
+                kWaitW = 7, kWaitSS = 8, kWaitDS = 9, kWaitT = 10, kWaitIssue = 11, kWaitUD = 12,
+                kWaitOFull = 13, kWaitOFree = 14 };
 // Limit of the waits for the CTA's own MMAs and copies in flight once it stops (these
 // complete on their own; the limit only keeps a broken device from holding the SM).
 constexpr uint64_t kDrainWaitNs = 2000000000ull;
@@ -124,10 +141,16 @@ struct TcParams {
     int64_t chain0;   // (sequence rank, v-head) chain of blockIdx.x = 0
     uint64_t wait_ns; // limit of every role's wait (ns)
     const int32_t *order;   // sequence of each rank (nullptr: rank = sequence index)
+    // Gated RMSNorm of the output in the store (gate == nullptr: plain store):
+    // o <- bf16(o / sqrt(mean(o^2) + eps) * w * silu(z)) per 128-element head vector.
+    const __nv_bfloat16 *gate;   // z, [T, Hv, 128] bf16
+    const void *norm_w;          // w, [128] (norm_w_dtype)
+    int norm_w_dtype;
+    float norm_eps;
 };
 
 struct Bars {
-    uint64_t tma[2], wdone, udone, d, s, qs, w, ss, ds, tw, tu, free_[2], oread, stg;
+    uint64_t tma[2], wdone, udone, d, s, qs, w, ss, ds, tw, tu, free_[2], oread, ofull, ofree;
 };
 
 __device__ __forceinline__ void issue_chunk(const CUtensorMap *qmap, const CUtensorMap *kmap,
@@ -222,8 +245,9 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
     // free[b]: chunk c's S-update batch (the last reader of stage c & 1 and P buffer c & 1) is done
     const uint32_t b_free0 = smem_u32(&bars.free_[0]), b_free1 = smem_u32(&bars.free_[1]);
     const uint32_t b_oread = smem_u32(&bars.oread);   // the prep warps have read O^T of a chunk
-    // the four prep warps' hand-offs around the output staging tile (two per output chunk)
-    const uint32_t b_stg = smem_u32(&bars.stg);
+    // output staging tile: ofull = the four prep warps have put output chunk j in it,
+    // ofree = the four store warps have read chunk j out of it
+    const uint32_t b_ofull = smem_u32(&bars.ofull), b_ofree = smem_u32(&bars.ofree);
     const uint64_t wl = p.wait_ns;
     float *dst_state = p.new_state + nh * kHeadDim * kHeadDim;
 
@@ -244,7 +268,8 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             mbar_init(b_free0, 1);
             mbar_init(b_free1, 1);
             mbar_init(b_oread, 4);
-            mbar_init(b_stg, 4);
+            mbar_init(b_ofull, 4);
+            mbar_init(b_ofree, kStoreWarps);
             abort_flag = 0;
             fence_mbar_init();
         }
@@ -417,22 +442,9 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
     } else if (warp <= 4) {
         // ------------------------------------------------------------ prep (chunk c + 1 while c runs)
         const int pt = tid - 32;    // 0..127
-        // Hand-off among the four prep warps around the staging tile: completion 2j of
-        // b_stg (parity 0) = the rows of the previous output chunk have left it, 2j + 1
-        // (parity 1) = output chunk j is in it.  False: another role gave up.  (No timer
-        // of its own: it only waits for the other three prep warps, and each of their
-        // waits is bounded and raises the flag when it gives up.)
-        auto stage_sync = [&](uint32_t parity) {
-            warp_arrive(b_stg, lane);
-            bool ok = true;
-            while (!mbar_try_wait_hint(b_stg, parity, kMaxSuspendNs)) {
-                if (*abort) {
-                    ok = false;
-                    break;
-                }
-            }
-            return __all_sync(0xffffffffu, ok);
-        };
+        // The previous chunk's output: O^T out of TMEM (TM_O then zeroed for the next delta
+        // batch), bf16 rows into the staging tile once the store warps have read the chunk
+        // before out of it, then handed to the store warps.  False: another role gave up.
         auto write_out = [&](int c) -> bool {
             uint32_t o[64];
             tmem_ld32(tmem_addr(tm, lane_base, TM_O), *reinterpret_cast<uint32_t(*)[32]>(o));
@@ -446,13 +458,10 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             }
             tc_fence_before();
             warp_arrive(b_oread, lane);
-            const int64_t t0 = s0 + static_cast<int64_t>(c) * kC;
-            const int nt = static_cast<int>(s1 - t0 < kC ? s1 - t0 : kC);
-            __nv_bfloat16 *so = reinterpret_cast<__nv_bfloat16 *>(sm + OFF_O);
-            if (!stage_sync(0)) return false;   // the previous chunk's rows have left the staging tile
+            if (c > 0 && !wait_warp(b_ofree, (c - 1) & 1, kWaitOFree, abort, wl)) return false;
             // two tokens per packed conversion (the single-value one runs at a quarter of the
             // rate and these warps share their SMSPs with the state split)
-            uint16_t *so16 = reinterpret_cast<uint16_t *>(so);
+            uint16_t *so16 = reinterpret_cast<uint16_t *>(sm + OFF_O);
 #pragma unroll
             for (int ii = 0; ii < 64; ii += 2) {
                 float o0, o1;
@@ -461,14 +470,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                 so16[ii * kHeadDim + row] = static_cast<uint16_t>(pk);
                 so16[(ii + 1) * kHeadDim + row] = static_cast<uint16_t>(pk >> 16);
             }
-            if (!stage_sync(1)) return false;
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int idx = pt + 128 * u, i = idx >> 4, c16 = idx & 15;
-                if (i < nt)
-                    *reinterpret_cast<uint4 *>(p.out + ((t0 + i) * p.Hv + h) * kHeadDim + c16 * 8) =
-                        *reinterpret_cast<const uint4 *>(sm + OFF_O + i * 256 + c16 * 16);
-            }
+            warp_arrive(b_ofull, lane);
             return true;
         };
         for (int c = 0; c < nch; ++c) {
@@ -543,6 +545,58 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         }
         // (a warp leaves the loop early only after a give-up, which has raised the flag)
         if (!*abort && nch > 0 && wait_warp(b_s, (nch - 1) & 1, kWaitS, abort, wl)) write_out(nch - 1);
+    } else if (warp >= kStoreWarp0) {
+        // ------------------------------------------------------------ output stores
+        // Store warp sw owns rows [16 sw, 16 sw + 16) of each output chunk, two rows per
+        // step (16 lanes, 16 bytes each: one coalesced 256-byte row).  With a gate, each
+        // row gets the gated RMSNorm of gdn_output_gate.cu (gated_rmsnorm16, the same
+        // arithmetic, so the result equals prefill followed by that pass bit for bit); the
+        // warp's gate rows of the next chunk are copied into shared memory (cp.async) as
+        // soon as it is done with the current one.  (Rolled loops: these warps share the
+        // instruction caches with the chain's critical path.)
+        const int sw = warp - kStoreWarp0;
+        const int l16 = lane & 15, half = lane >> 4;
+        const uint32_t zbase = sbase + OFF_Z + sw * (kStoreRows * 256);
+        float wv[8] = {};
+        if (p.gate) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) wv[i] = load_scalar(p.norm_w, l16 * 8 + i, p.norm_w_dtype);
+        }
+        auto fetch_gate = [&](int c) {
+            const int64_t t0 = s0 + static_cast<int64_t>(c) * kC;
+            const int nt = static_cast<int>(s1 - t0 < kC ? s1 - t0 : kC);
+#pragma unroll 1
+            for (int u = 0; u < kStoreRows / 2; ++u) {
+                const int r = 2 * u + half, i = kStoreRows * sw + r;
+                if (i < nt)
+                    cp_async16(zbase + r * 256 + l16 * 16, p.gate + ((t0 + i) * p.Hv + h) * kHeadDim + l16 * 8, 16);
+            }
+            cp_async_commit();
+        };
+        if (p.gate && nch > 0) fetch_gate(0);
+        for (int c = 0; c < nch; ++c) {
+            const int64_t t0 = s0 + static_cast<int64_t>(c) * kC;
+            const int nt = static_cast<int>(s1 - t0 < kC ? s1 - t0 : kC);
+            const bool ok = wait_warp(b_ofull, c & 1, kWaitOFull, abort, wl);
+            if (p.gate) {
+                cp_async_wait<0>();      // (also after a give-up: nothing left in flight)
+                __syncwarp();
+            }
+            if (!ok) break;
+#pragma unroll 2
+            for (int u = 0; u < kStoreRows / 2; ++u) {
+                const int r = 2 * u + half, i = kStoreRows * sw + r;
+                uint4 y = *reinterpret_cast<const uint4 *>(sm + OFF_O + i * 256 + l16 * 16);
+                if (p.gate) {            // (every lane: the RMS shuffles span the 16-lane group)
+                    const uint4 zv = *reinterpret_cast<const uint4 *>(sm + OFF_Z + sw * (kStoreRows * 256) +
+                                                                      r * 256 + l16 * 16);
+                    y = gated_rmsnorm16(y, zv, wv, p.norm_eps);
+                }
+                if (i < nt) *reinterpret_cast<uint4 *>(p.out + ((t0 + i) * p.Hv + h) * kHeadDim + l16 * 8) = y;
+            }
+            warp_arrive(b_ofree, lane);
+            if (p.gate && c + 1 < nch) fetch_gate(c + 1);
+        }
     } else {
         // ------------------------------------------------------------ state path (chunk c)
         // Two halves of four warps (one per TMEM lane quadrant): half hs owns state
@@ -835,7 +889,9 @@ cudaError_t launch_prefill_tc(const PrefillArgs &p, void *workspace, cudaStream_
         !make_tmap_thd_bf16(&km, p.k, p.total_tokens, p.Hq) ||
         !make_tmap_thd_bf16(&vm, p.v, p.total_tokens, p.Hv))
         return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         SMEM_BYTES_GATED);
+    const uint32_t smem = p.out_gate ? SMEM_BYTES_GATED : SMEM_BYTES;
     if (e != cudaSuccess) return e;
     const uint64_t limit = g_wait_limit_ns.load(std::memory_order_relaxed);
     const uint64_t wait_ns = limit ? limit : kDefaultWaitNs;
@@ -873,8 +929,9 @@ cudaError_t launch_prefill_tc(const PrefillArgs &p, void *workspace, cudaStream_
         cudaError_t er = launch_chunk_prep(p, ws_T, ws_P, ws_g, st, c0, c1);
         if (er != cudaSuccess) return er;
         TcParams tp{p.state, p.cu_seqlens, p.num_seqs, p.total_tokens, p.Hq, p.Hv, p.scale,
-                    static_cast<__nv_bfloat16 *>(p.out), p.new_state, ws_T, ws_g, ws_P, c0, wait_ns, order};
-        prefill_tc_kernel<<<static_cast<unsigned>(c1 - c0), kThreads, SMEM_BYTES, st>>>(qm, km, vm, tp);
+                    static_cast<__nv_bfloat16 *>(p.out), p.new_state, ws_T, ws_g, ws_P, c0, wait_ns, order,
+                    static_cast<const __nv_bfloat16 *>(p.out_gate), p.norm_w, p.norm_w_dtype, p.norm_eps};
+        prefill_tc_kernel<<<static_cast<unsigned>(c1 - c0), kThreads, smem, st>>>(qm, km, vm, tp);
         return cudaGetLastError();
     };
     if (tail > 0) {

@@ -57,6 +57,7 @@ def test_prefill_with_output_gate(method):
     ([700, 129, 64, 1], 4, 8, torch.float32),          # partial chunks, a one-token sequence
     ([300, 128, 257, 64, 200], 16, 32, torch.bfloat16),  # 160 chains: the wave split
     ([256, 0, 191, 64, 300], 16, 32, torch.float32),     # an empty sequence among them
+    ([1500, 4096, 999, 2048], 16, 32, torch.bfloat16),   # many chunks per chain through the store warps
 ])
 def test_gated_prefill_is_bit_identical_to_two_calls(lengths, Hq, Hv, wdtype):
     """kernel(..., output_gate=) (gdn_prefill_gated; on tcgen05 the gating is applied in the

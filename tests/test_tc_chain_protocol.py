@@ -1,9 +1,9 @@
 """CPU model of the mbarrier protocol of the tcgen05 chain kernel
 (fastaf_kernel_b200/csrc/gdn_prefill_tc.cu), run under random schedules.
 
-The kernel hands every chunk between five roles -- the MMA-issuing thread, the copy
-thread, four prep warps and eight state warps -- through mbarriers only (no block-wide
-barrier in the chunk loop).  The model runs each warp as a coroutine that follows the
+The kernel hands every chunk between six roles -- the MMA-issuing thread, the copy
+thread, four prep warps, eight state warps and four output-store warps -- through
+mbarriers only (no block-wide barrier in the chunk loop).  The model runs each warp as a coroutine that follows the
 kernel's waits, reads, writes and arrives in the kernel's order; MMA batches and
 copies are asynchronous events.  The tensor pipe is in order (tcgen05.mma and
 tcgen05.commit issued by one thread complete in issue order, a commit arriving once
@@ -22,7 +22,8 @@ Each schedule checks:
 Buffers: shared-memory stages (K, Q, V, P, gates) x 2, the T' and T'' tiles, -W hi/lo
 and (Gamma Q)^T (per TMEM lane quadrant of the warp that writes them); TMEM S (per
 state half and quadrant), the [128, 256) hi/lo/delta region in 16-column blocks,
-W^T, [U | X] and O^T (per quadrant).
+W^T, [U | X] and O^T (per quadrant); the output staging tile (per column block, written
+by the prep warp of that TMEM lane quadrant and read by every store warp).
 
 The kernel's barrier counts are read from the source and compared with the model's.
 Planted protocol mistakes (a missing condition or wait) must be caught.
@@ -87,7 +88,7 @@ class Sim:
         self.pipe = []        # in-order tensor pipe: ("mma", reads, writes) / ("commit", bar)
         self.copies = []      # in-flight copies: (part, tag, bar)
         counts = dict(tma0=1, tma1=1, wdone=1, udone=1, d=1, s=1, qs=4, w=4, ss=8, ds=8, tw=1, tu=1,
-                      free0=1, free1=1, oread=4, stg=4)
+                      free0=1, free1=1, oread=4, ofull=4, ofree=4)
         self.counts = counts
         self.b = {k: Bar(k, v) for k, v in counts.items()}
 
@@ -208,9 +209,9 @@ def mma10(sim, c):   # S += delta'^T K, O^T += delta^T P^T
 # ------------------------------------------------------------------ roles
 # A role yields ("wait", bar, k) for a bounded, abort-aware wait (it receives True, or
 # False once it gave up or saw the abort flag), ("drain", bar, k) for a wait on its own
-# asynchronous work (always satisfied in the end), ("sync", bar, k) for the prep warps'
-# staging hand-off (no timer of its own: false only once the flag is up), "spin" for a
-# probe round of the issuing thread, or None to let others run.
+# asynchronous work (always satisfied in the end), ("wait_forever", bar, k) for a planted
+# wait without the abort check, "spin" for a probe round of the issuing thread, or None to
+# let others run.
 def issuer(sim):
     b, nch, plant = sim.b, sim.nch, sim.plant
     n6w = n6u = n8 = n10 = 0
@@ -283,24 +284,18 @@ def copier(sim):
 def prep(sim, q):
     who = f"prep{q}"
     out_bar = "s"
-    nout = [0]
-    sync = "wait_forever" if sim.plant == "named_barrier" else "sync"
 
     def write_out(c):
         sim.read(("O", q), ("out", c), who)
         yield None
         sim.write(("O", q), ("zero", c + 1), who)
         sim.b["oread"].arrive()
-        j = nout[0]
-        nout[0] += 1
-        sim.b["stg"].arrive()
-        if not (yield (sync, "stg", 2 * j)):
+        if c > 0 and sim.plant != "no_ofree_wait" and not (yield ("wait", "ofree", c - 1)):
             return False
         yield None                                  # bf16 rows into the staging tile
-        sim.b["stg"].arrive()
-        if not (yield (sync, "stg", 2 * j + 1)):
-            return False
-        yield None                                  # staging tile -> global rows
+        sim.write(("STG", q), ("out", c), who)
+        yield None
+        sim.b["ofull"].arrive()
         return True
 
     for c in range(sim.nch):
@@ -332,6 +327,22 @@ def prep(sim, q):
                 break
     if not sim.abort and sim.nch and (yield ("wait", out_bar, sim.nch - 1)):
         yield from write_out(sim.nch - 1)
+
+
+def store(sim, sw):
+    who = f"store{sw}"
+    handoff = "wait_forever" if sim.plant == "unbounded_handoff" else "wait"
+    for c in range(sim.nch):
+        yield None                                  # gate rows of chunk c into registers
+        if not (yield (handoff, "ofull", c)):
+            break
+        for q in Q4:                                # the loop over the chunk's rows reads the
+            sim.read(("STG", q), ("out", c), who)   # tile from its first step to its last
+        yield None                                  # (gated) rows to global
+        yield None
+        for q in Q4:
+            sim.read(("STG", q), ("out", c), who)
+        sim.b["ofree"].arrive()
 
 
 def state(sim, hs, q):
@@ -376,6 +387,7 @@ def run(nch, seed, plant=None, max_steps=400000, timeouts=False):
     roles = {"issuer": issuer(sim), "copier": copier(sim)}
     roles.update({f"prep{q}": prep(sim, q) for q in Q4})
     roles.update({f"state{hs}.{q}": state(sim, hs, q) for hs in (0, 1) for q in Q4})
+    roles.update({f"store{sw}": store(sim, sw) for sw in Q4})
     waiting = {}    # role -> (kind, bar, k)
     done = set()
 
@@ -406,8 +418,6 @@ def run(nch, seed, plant=None, max_steps=400000, timeouts=False):
                 if sim.b[bar].test(k, n):
                     ready.append(("role", n, True))
                 elif kind == "wait" and (sim.abort or (timeouts and rng.random() < 0.002)):
-                    ready.append(("role", n, False))
-                elif kind == "sync" and sim.abort:
                     ready.append(("role", n, False))
                 continue
             ready.append(("role", n, None))
@@ -448,7 +458,7 @@ def test_protocol_random_schedules(nch):
                 assert sim.tags[("S", hs, q)] == ("S", nch)
 
 
-@pytest.mark.parametrize("plant", ["w_early", "u_early", "no_free_wait", "no_oread"])
+@pytest.mark.parametrize("plant", ["w_early", "u_early", "no_free_wait", "no_oread", "no_ofree_wait"])
 def test_planted_protocol_mistakes_are_caught(plant):
     with pytest.raises(ProtocolError):
         for seed in range(200):
@@ -466,12 +476,12 @@ def test_give_up_path_terminates_with_nothing_in_flight(nch):
     assert aborted > 30
 
 
-@pytest.mark.parametrize("plant,nch,seeds", [("named_barrier", 4, 400),
+@pytest.mark.parametrize("plant,nch,seeds", [("unbounded_handoff", 4, 400),
                                               ("copy_drain_on_own_failure_only", 1, 2000)])
 def test_planted_give_up_mistakes_are_caught(plant, nch, seeds):
-    """A staging hand-off that cannot give up (a named barrier) deadlocks once another
-    prep warp stopped; a copy thread that drains only after its own wait failed leaves
-    copies in flight when another role gave up."""
+    """A staging hand-off that cannot give up (a wait without the abort check) deadlocks
+    once a prep warp stopped; a copy thread that drains only after its own wait failed
+    leaves copies in flight when another role gave up."""
     with pytest.raises(ProtocolError):
         for seed in range(seeds):
             run(nch, 31000 + seed, plant, timeouts=True)
@@ -480,5 +490,7 @@ def test_planted_give_up_mistakes_are_caught(plant, nch, seeds):
 def test_barrier_counts_match_the_kernel():
     """The kernel's mbar_init counts equal the model's."""
     src = open(KERNEL).read()
-    inits = {name[2:]: int(n) for name, n in re.findall(r"mbar_init\((b_\w+), (\d+)\)", src)}
+    consts = {k: int(v) for k, v in re.findall(r"constexpr int (k\w+) = (\d+);", src)}
+    inits = {name[2:]: int(n) if n.isdigit() else consts[n]
+             for name, n in re.findall(r"mbar_init\((b_\w+), (\w+)\)", src)}
     assert inits == Sim(1).counts
