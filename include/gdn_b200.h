@@ -190,7 +190,9 @@ GDN_API int gdn_output_gate(void *output, const void *gate, const void *weight, 
 
 /* gdn_prefill_flags followed by gdn_output_gate on the output, in one call (gate:
  * bf16 [T, Hv, D], 16-byte aligned; norm_weight [D] in norm_weight_dtype).
- * Bit-identical to the two calls.  No counterpart in the reference. */
+ * Bit-identical to the two calls.  On GDN_PREFILL_TCGEN05 the gating is applied in the
+ * chains' output stores (the output is written once); the other methods run the
+ * gdn_output_gate pass after the prefill.  No counterpart in the reference. */
 GDN_API int gdn_prefill_gated(const void *q, const void *k, const void *v, const float *state,
                       const void *A_log, const void *a, const void *dt_bias, const void *b,
                       const int32_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
@@ -207,8 +209,8 @@ GDN_API int gdn_prefill_gated(const void *q, const void *k, const void *v, const
 GDN_API int gdn_prefill_resolve(int64_t total_tokens, int64_t num_seqs, int method);
 
 /* Kernel launches of one tcgen05 prefill through the pooled-workspace entry points
- * (gdn_prefill, gdn_prefill_ex, gdn_prefill_flags, gdn_prefill_strided, gdn_prefill_gated
- * without its gating pass) on a device with `num_sms` SMs: 2 (chunk prep, chains), or 4
+ * (gdn_prefill, gdn_prefill_ex, gdn_prefill_flags, gdn_prefill_strided, gdn_prefill_gated)
+ * on a device with `num_sms` SMs: 2 (chunk prep, chains), or 4
  * when the last partial wave of (sequence, v-head) chains is split onto the library's
  * second stream (more chains than SMs, chains mod SMs > 0 and a whole number of prep
  * CTAs); plus 1 when there are at least 2 sequences and more chains than SMs: a kernel
