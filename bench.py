@@ -578,8 +578,9 @@ def main():
     T = N_SEQS * SEQ_LEN
     kernel_name = fk.prefill_method(T, args.method, N_SEQS)
     # the tcgen05 path is two launches per step (chunk prep, then the chains), four when
-    # the library splits off the last partial wave of chains onto its second stream (the
-    # library's own rule, gdn_prefill_tc_launches)
+    # the library splits off the last partial wave of chains onto its second stream, one
+    # more when it ranks the sequences longest first (the library's own rule,
+    # gdn_prefill_tc_launches: five for 16 x 8192 on 148 SMs)
     launches_per_step = 1
     if kernel_name == "tcgen05":
         from fastaf_kernel_b200 import _lib
