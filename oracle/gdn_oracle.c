@@ -1,8 +1,8 @@
 /*
  * CPU oracle for the Gated DeltaNet prefill/decode path -- TEST INFRASTRUCTURE.
  *
- * This is the checker and the timed CPU baseline, never the product: only the
- * tests, the smoke check and bench.py's CPU legs load it.
+ * It is what the GPU results are compared against and the timed CPU baseline, never
+ * the product: only the tests, the smoke check and bench.py's CPU legs load it.
  *
  * A plain-C, fp32, token-serial restatement of the reference's torch
  * implementation (solution/gdn_baseline_torch.py:12-91) with the head-count
