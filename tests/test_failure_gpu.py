@@ -78,26 +78,41 @@ def test_mbarrier_wait_nobody_arrives_gives_up():
 
 
 @pytest.mark.gpu
-def test_chain_waits_run_out_then_next_call_is_correct():
+@pytest.mark.parametrize("gated", [False, True])
+def test_chain_waits_run_out_then_next_call_is_correct(gated):
     """With a 1 us limit the tcgen05 chains' waits run out: the call returns, the status
     word says GDN_ERR_DEVICE_TIMEOUT (and is cleared by reading it), and the next call
-    with the default limit -- which allocates the same tensor memory -- matches the oracle."""
+    with the default limit -- which allocates the same tensor memory -- matches the oracle.
+    Gated: the output-store warps also have gate-row copies in flight when they give up."""
     lib = _lib.load()
     x = W.prefill_inputs([700, 300, 513], seed=91, Hq=16, Hv=32)
     g = _gpu(x)
+    kw = {}
+    if gated:
+        gen = torch.Generator(device=DEV).manual_seed(92)
+        kw = dict(output_gate=torch.randn((g["q"].shape[0], 32, 128), generator=gen, device=DEV).to(torch.bfloat16),
+                  norm_weight=torch.rand(128, generator=gen, device=DEV) + 0.5)
+    run = lambda: fk.kernel(g["q"], g["k"], g["v"], g["state"], g["A_log"], g["a"], g["dt_bias"], g["b"],
+                            g["cu_seqlens"], g["scale"], method="tcgen05", **kw)
     prev = lib.gdn_set_wait_limit_ns(1000)
     try:
-        _run(g, "tcgen05")
+        run()
         with pytest.raises(_lib.GdnError) as ei:
             fk.device_status()
         assert ei.value.status == _lib.GDN_ERR_DEVICE_TIMEOUT
     finally:
         lib.gdn_set_wait_limit_ns(prev)
     fk.device_status()    # cleared
-    o, s = _run(g, "tcgen05")
+    o, s = run()
     fk.device_status()
-    ro, rs = _oracle(x)
-    assert_parity(o.cpu(), ro, s.cpu(), rs)
+    if gated:
+        o_plain, s_plain = _run(g, "tcgen05")
+        assert torch.equal(s, s_plain)
+        fk.output_gate(o_plain, kw["output_gate"], kw["norm_weight"], 1e-6)
+        assert torch.equal(o, o_plain)
+    else:
+        ro, rs = _oracle(x)
+        assert_parity(o.cpu(), ro, s.cpu(), rs)
 
 
 @pytest.mark.gpu
