@@ -792,8 +792,12 @@ cudaError_t launch_chain_order(const int32_t *cu_seqlens, int64_t num_seqs, int6
     return cudaGetLastError();
 }
 
+// The ranking compares every pair of sequences (a few microseconds for thousands of
+// sequences); beyond kMaxRankedSeqs the batch keeps sequence order.
+constexpr int64_t kMaxRankedSeqs = 65536;
+
 bool prefill_tc_orders_chains(int64_t num_seqs, int Hv, int sms) {
-    return num_seqs >= 2 && sms > 0 && num_seqs * Hv > sms;
+    return num_seqs >= 2 && num_seqs <= kMaxRankedSeqs && sms > 0 && num_seqs * Hv > sms;
 }
 
 int64_t prefill_tc_overlap_tail(int64_t chains, int sms, int heads_per_prep_cta) {

@@ -213,7 +213,7 @@ GDN_API int gdn_prefill_resolve(int64_t total_tokens, int64_t num_seqs, int meth
  * on a device with `num_sms` SMs: 2 (chunk prep, chains), or 4
  * when the last partial wave of (sequence, v-head) chains is split onto the library's
  * second stream (more chains than SMs, chains mod SMs > 0 and a whole number of prep
- * CTAs); plus 1 when there are at least 2 sequences and more chains than SMs: a kernel
+ * CTAs); plus 1 when there are 2 to 65,536 sequences and more chains than SMs: a kernel
  * that ranks the sequences longest first on the device, so the chains of the longest
  * sequences start first (the results do not depend on the order).  0 for invalid
  * shapes.  Host arithmetic only.  No counterpart in the reference. */

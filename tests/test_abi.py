@@ -112,6 +112,7 @@ def test_error_maps_to_python_exceptions():
     (13, 4, 12, 148, 5),     # one v-head per prep CTA: tail of 8; sequences ranked
     (16, 16, 32, 147, 3),    # a tail of 71 is not a whole number of two-head prep CTAs
     (1, 4, 512, 148, 4),     # one sequence of 512 chains: a tail of 68 split off, nothing to rank
+    (65537, 2, 4, 148, 4),   # more sequences than are ranked: index order (tail of 40 split off)
     (1, 3, 4, 148, 0),       # invalid head counts
 ])
 def test_prefill_tc_launch_count_rule(n, hq, hv, sms, launches):
