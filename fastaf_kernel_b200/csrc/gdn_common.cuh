@@ -1,6 +1,8 @@
 // gdn_common.cuh -- shared device helpers for the Gated DeltaNet kernels (sm_100a).
 #pragma once
 
+#include "gdn_chunk_common.cuh"
+
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -61,38 +63,51 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     return *reinterpret_cast<uint32_t *>(&h);
 }
 
+__device__ __forceinline__ uint64_t fma_f2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+// The hardware's tanh approximation (MUFU; a few units of 2^-11 relative).
+__device__ __forceinline__ float tanh_approx(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // Gated RMSNorm of one 128-element bf16 vector held by an aligned group of 16 lanes,
 // 8 elements (one 16-byte word) each: o / sqrt(mean(o^2) + eps) * w * silu(z), fp32,
 // rounded to bf16.  ow / zw are this lane's words of o and z, wv its 8 weights.  Every
-// lane of the warp must call it (full-warp shuffles).  The reciprocal square root, the
-// exponential and the division of silu use the hardware approximations (rsqrtf, __expf,
-// __fdividef: a few ulp in fp32, far below the bf16 rounding of the result), so the
-// tcgen05 prefill's output-store warps keep up with a chunk in their shared budget; the
-// standalone pass uses this same routine, so both give the same bits.
+// lane of the warp must call it (full-warp shuffles).  Built for few instructions, since
+// the tcgen05 prefill's output-store warps run it beside the chain's critical path: packed
+// f32x2 arithmetic, the hardware reciprocal square root, and sigmoid(z) = (1 + tanh(z/2))/2
+// with the hardware tanh -- a few units of 2^-11 relative, below the bf16 rounding of the
+// result.  The standalone pass uses this same routine, so both give the same bits.
 __device__ __forceinline__ uint4 gated_rmsnorm16(uint4 ov, uint4 zv, const float (&wv)[8], float eps) {
     const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w}, zw[4] = {zv.x, zv.y, zv.z, zv.w};
-    float x[8], g[8];
+    uint64_t x2[4];
+    uint64_t ss2 = f2(0.0f, 0.0f);
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-        x[2 * e] = bf16_lo(ow[e]); x[2 * e + 1] = bf16_hi(ow[e]);
-        g[2 * e] = bf16_lo(zw[e]); g[2 * e + 1] = bf16_hi(zw[e]);
+        x2[e] = f2(bf16_lo(ow[e]), bf16_hi(ow[e]));
+        ss2 = fma_f2(x2[e], x2[e], ss2);
     }
-    float ss = 0.0f;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) ss = fmaf(x[e], x[e], ss);
+    float sa, sb;
+    unf2(ss2, sa, sb);
+    float ss = sa + sb;
 #pragma unroll
     for (int m = 1; m < 16; m <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
     const float inv = rsqrtf(ss * (1.0f / 128.0f) + eps);
+    const uint64_t inv2 = f2(inv, inv), half2 = f2(0.5f, 0.5f);
     uint32_t r[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-        float y[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const int i = 2 * e + u;
-            y[u] = x[i] * inv * wv[i] * __fdividef(g[i], 1.0f + __expf(-g[i]));
-        }
-        r[e] = pack_bf16x2(y[0], y[1]);
+        const float g0 = bf16_lo(zw[e]), g1 = bf16_hi(zw[e]);
+        const uint64_t g2 = f2(g0, g1);
+        const uint64_t sg2 = fma_f2(f2(tanh_approx(0.5f * g0), tanh_approx(0.5f * g1)), half2, half2);
+        float y0, y1;
+        unf2(mul_f2(mul_f2(mul_f2(x2[e], inv2), f2(wv[2 * e], wv[2 * e + 1])), mul_f2(g2, sg2)), y0, y1);
+        r[e] = pack_bf16x2(y0, y1);
     }
     return make_uint4(r[0], r[1], r[2], r[3]);
 }
