@@ -51,10 +51,18 @@ def test_decode_instances_keep_three_ctas_per_sm(tmp_path):
         assert st == 0 and ld == 0, f"{name}: spills {st}/{ld} bytes"
 
 
+def _chain_threads():
+    src = open(os.path.join(B.CSRC, "gdn_prefill_tc.cu")).read()
+    return int(re.search(r"constexpr int kThreads = (\d+);", src).group(1))
+
+
 def test_chain_kernel_does_not_spill(tmp_path):
+    """One CTA per SM: the CTA's warps at the kernel's register count (allocated in steps
+    of 8 a thread) must fit the 65,536 registers, with nothing spilled."""
+    threads = _chain_threads()
     rep = _ptxas_report("gdn_prefill_tc.cu", tmp_path)
     chain = {k: v for k, v in rep.items() if "prefill_tc_kernel" in k}
     assert chain, sorted(rep)
     for name, (regs, st, ld) in chain.items():
-        assert regs * 448 <= 65536, f"{name}: {regs} registers x 448 threads exceed the SM"
+        assert (regs + 7) // 8 * 8 * threads <= 65536, f"{name}: {regs} registers x {threads} threads exceed the SM"
         assert st == 0 and ld == 0, f"{name}: spills {st}/{ld} bytes"
