@@ -4,10 +4,11 @@
 //
 //   out = o / sqrt(mean(o^2) + eps) * w * silu(z),   silu(z) = z / (1 + exp(-z)),
 //
-// per 128-element head vector, in fp32 from the bf16 o and z, rounded to bf16.  It
-// reads and writes the output once (in place); 16 lanes own one vector, 8 elements
-// (one 16-byte load) each, and reduce the sum of squares with a 16-lane butterfly
-// (gated_rmsnorm16, which the tcgen05 prefill's fused output store shares).
+// per 128-element head vector, in fp32 from the bf16 o and z (sigmoid from the hardware
+// tanh, the hardware reciprocal square root), rounded to bf16.  It reads and writes the
+// output once (in place); 16 lanes own one vector, 8 elements (one 16-byte load) each,
+// and reduce the sum of squares with a 16-lane butterfly (gated_rmsnorm16, which the
+// tcgen05 prefill's fused output store shares, so both give the same bits).
 #include "gdn_common.cuh"
 #include "gdn_launch.h"
 

@@ -176,7 +176,9 @@ GDN_API int gdn_prefill_noalloc(const void *q, const void *k, const void *v, con
  * Gated RMSNorm of the recurrence output, in place:
  *   output <- bf16(output / sqrt(mean(output^2) + eps) * weight * silu(gate))
  * over every 128-element head vector (num_vectors = tokens * v-heads), in fp32 from
- * the bf16 output and gate.  Gated DeltaNet layers apply it between the recurrence
+ * the bf16 output and gate (the reciprocal square root and the sigmoid of silu use the
+ * hardware approximations: a few units of 2^-11 relative, below the bf16 rounding of the
+ * result).  Gated DeltaNet layers apply it between the recurrence
  * and the output projection; call it on the output of gdn_prefill* / gdn_decode* on
  * the same stream.
  *   output   bf16 [num_vectors, head_size], 16-byte aligned (read and written)
