@@ -134,3 +134,28 @@ def test_device_resident_cu_seqlens_is_checked_on_the_device(method, bad):
     fk.device_status()
     ro, rs = _oracle(x)
     assert_parity(o.cpu(), ro, s.cpu(), rs)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bad_at,value", [(3, 10**6), (5, -7), (7, 100)])
+def test_device_cu_seqlens_check_with_the_sequence_ranking(bad_at, value):
+    """Enough chains (10 sequences x 32 v-heads = 320 > 148 SMs) that the pooled tcgen05
+    call ranks its sequences on the device before the chains: with one malformed entry
+    (past T, negative, or below its predecessor) the ranking still gives a permutation of
+    the clamped lengths, every access stays in bounds, the error is recorded, and the next
+    good call matches the oracle."""
+    lengths = [300, 64, 1, 257, 128, 65, 500, 0, 192, 129]
+    x = W.prefill_inputs(lengths, seed=93, Hq=16, Hv=32)
+    g = _gpu(x)
+    cu = [0]
+    for L in lengths:
+        cu.append(cu[-1] + L)
+    cu[bad_at] = value
+    _run(g, "tcgen05", cu=torch.tensor(cu, dtype=torch.int32, device=DEV))
+    with pytest.raises(ValueError, match="cu_seqlens"):
+        fk.device_status()
+    fk.device_status()    # cleared
+    o, s = _run(g, "tcgen05")
+    fk.device_status()
+    ro, rs = _oracle(x)
+    assert_parity(o.cpu(), ro, s.cpu(), rs)
